@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Benchmark: sparse NNUE feature transformer forward + backward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Workload (the reference's headline configuration
+and [3]): Full_Threats+HalfKAv2_hm^ feature transformer, global batch 65536
+positions, L1 = 1040 + 8 PSQT columns (C = 1048), table 85296 x 1048 fp32,
+K = 160 padded int32 indices per perspective.  One step = forward of both
+perspectives + backward (dense weight gradient written once, bias gradient)
+and, for N > 1, the fp32 allreduce-mean of both gradients over NVLink.  The
+global batch is split evenly over ranks (strong scaling, like the reference's
+DDP path, src/train/common.py:256-263).
+
+Inputs are synthetic: seeded random positions (stockfish_trainer_b200.positions)
+encoded by the native restatement of the reference's feature functions,
+W ~ N(0, 0.01), bias 0, dOut ~ N(0, 1).  All inputs (idx 84 MB, W 357 MB,
+dOut 550 MB) are larger than the 126 MB L2, so no flush between steps.
+
+Prints ONE JSON line on rank 0.  `--impl reference` times the CPU restatement
+of the reference path (oracle/, the reference has no CPU path of its own) on
+this host's cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "positions/s FT fwd+bwd @B=65536 L1=1040, 1/2/4/8 B200; % HBM roofline"
+FEATURE_SET = "Full_Threats+HalfKAv2_hm^"
+L1, NPSQT = 1040, 8
+C = L1 + NPSQT
+DATA = ("synthetic: seeded random positions (kings + U{0..30} pieces), indices from the native restatement "
+        "of the reference feature functions; W~N(0,0.01), bias=0, dOut~N(0,1)")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=65536, help="global batch (positions)")
+    p.add_argument("--seed", type=int, default=2024)
+    p.add_argument("--feature-set", default=FEATURE_SET)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline time budget")
+    return p.parse_args()
+
+
+def hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.rows = []
+        self.marks = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "-i", str(gpu_index), "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def mark(self):
+        self.marks.append(time.time())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        t0, t1 = (self.marks + [0, 0])[:2] if len(self.marks) >= 2 else (0, float("inf"))
+        inside = [r for t, r in self.rows if t0 - 0.15 <= t <= t1 + 0.15] or [r for _, r in self.rows]
+        sm, smax, reasons = [], [], set()
+        for r in inside:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(self.REASONS, r[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference path, all host threads)
+# ---------------------------------------------------------------------------
+def cpu_baseline(white, black, W_np, seed, budget_s, per_step=None):
+    import oracle
+
+    T = W_np.shape[0]
+    n = min(len(white), per_step or 4096)
+    rng = np.random.default_rng(seed + 99)
+    g0 = rng.standard_normal((n, C), dtype=np.float32)
+    g1 = rng.standard_normal((n, C), dtype=np.float32)
+    bias = np.zeros(C, np.float32)
+    w, b = np.ascontiguousarray(white[:n]), np.ascontiguousarray(black[:n])
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        oracle.ft_forward(w, W_np, bias)
+        oracle.ft_forward(b, W_np, bias)
+        oracle.ft_backward_pair(w, b, g0, g1, T)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s or len(times) >= 10:
+            break
+    t_med = statistics.median(times)
+    return {
+        "value": n / t_med,
+        "unit": "positions/s",
+        "cores": oracle.max_threads(),
+        "kind": "port",
+        "sample": f"{n} positions of the headline workload (both perspectives, fwd + bwd incl. the two dense "
+                  f"dW the reference allocates), median of {len(times)} reps, C oracle with OpenMP",
+        "ms_per_sample": t_med * 1e3,
+    }
+
+
+def base_config(args, world, b_rank, T, K, nnz=None):
+    cfg = {
+        "workload": f"{args.feature_set} feature transformer fwd+bwd, both perspectives, dense dW + dB"
+                    + (", fp32 allreduce-mean" if world > 1 else ""),
+        "feature_set": args.feature_set,
+        "global_batch": args.batch,
+        "batch_per_gpu": b_rank,
+        "L1": L1,
+        "psqt": NPSQT,
+        "num_inputs": T,
+        "max_active": K,
+        "parallelism": f"dp{world}",
+        "l2": "inputs larger than L2 (126 MB), no flush",
+    }
+    if nnz is not None:
+        cfg["nnz_per_step"] = nnz
+    return cfg
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return 0
+    from stockfish_trainer_b200 import positions
+
+    fid, T, K = positions.feature_set_info(args.feature_set)
+    n = 2048
+    white, black, _ = positions.synthetic_batch(n, args.feature_set, seed=args.seed)
+    rng = np.random.default_rng(args.seed)
+    W_np = (rng.standard_normal((T, C), dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    import oracle
+
+    g0 = rng.standard_normal((n, C), dtype=np.float32)
+    g1 = rng.standard_normal((n, C), dtype=np.float32)
+    bias = np.zeros(C, np.float32)
+
+    def sample_step():
+        oracle.ft_forward(white, W_np, bias)
+        oracle.ft_forward(black, W_np, bias)
+        oracle.ft_backward_pair(white, black, g0, g1, T)
+
+    for _ in range(args.warmup):
+        sample_step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        sample_step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = n * len(times) / total
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "positions/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total / len(times) * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": DATA,
+        "config": base_config(args, world, args.batch // max(world, 1), T, K),
+        "cpu_baseline": {"value": value, "unit": "positions/s", "cores": oracle.max_threads(), "kind": "port",
+                         "sample": f"each step: {n} positions of the headline workload, fwd + bwd of both "
+                                   "perspectives (C restatement of the reference kernels, OpenMP)"},
+        "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from stockfish_trainer_b200 import SparseLinearPairFunction, _native, ddp, positions
+    from stockfish_trainer_b200.feature_transformer import ops
+
+    rt = ddp.init_from_env("nccl", timeout_s=180.0)
+    rank, world = rt.rank, rt.world_size
+    dev = torch.device("cuda", rt.local_rank)
+    torch.cuda.set_device(dev)
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+
+    fid, T, K = positions.feature_set_info(args.feature_set)
+    first, b_rank = ddp.shard(args.batch, rank, world)
+    white, black, _ = positions.synthetic_batch(b_rank, args.feature_set, seed=args.seed, first=first)
+    nnz_rank = int((white >= 0).sum() + (black >= 0).sum())
+
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    W = torch.randn(T, C, device=dev, generator=gen) * 0.01
+    bias = torch.zeros(C, device=dev)
+    gen_r = torch.Generator(device=dev).manual_seed(args.seed + 1000 + rank)
+    g0 = torch.randn(b_rank, C, device=dev, generator=gen_r)
+    g1 = torch.randn(b_rank, C, device=dev, generator=gen_r)
+    i0 = torch.from_numpy(white).to(dev)
+    i1 = torch.from_numpy(black).to(dev)
+    out0 = torch.empty(b_rank, C, device=dev)
+    out1 = torch.empty_like(out0)
+    ws = ops.alloc_workspace(b_rank, K, T, C, 2, dev)
+    grads = ddp.GradientBuffer(T, C, dev)
+
+    n_ev = 5
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(max(args.steps, 1))]
+
+    def step(e=None):
+        if e:
+            e[0].record()
+        ops.forward_pair_into(i0, i1, W, bias, out0, out1)
+        if e:
+            e[1].record()
+        ops.backward_prepare(i0, i1, T, C, ws)
+        if e:
+            e[2].record()
+        ops.backward_apply(g0, g1, b_rank, K, grads.weight, grads.bias, False, ws)
+        if e:
+            e[3].record()
+        grads.allreduce_mean(world)
+        if e:
+            e[4].record()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+
+    clocks = ClockSampler(rt.local_rank) if rank == 0 else None
+    time.sleep(0.3)  # let the sampler start
+    barrier()
+    l0 = _native.launch_count()
+    if clocks:
+        clocks.mark()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for k in range(args.steps):
+        step(ev[k])
+    end.record()
+    barrier()
+    if clocks:
+        clocks.mark()
+    launches = _native.launch_count() - l0
+    ms_local = start.elapsed_time(end)
+    ms = max_over_ranks(ms_local)
+    phases = {
+        "forward": [e[0].elapsed_time(e[1]) for e in ev[: args.steps]],
+        "backward_prepare": [e[1].elapsed_time(e[2]) for e in ev[: args.steps]],
+        "backward_apply": [e[2].elapsed_time(e[3]) for e in ev[: args.steps]],
+        "allreduce": [e[3].elapsed_time(e[4]) for e in ev[: args.steps]],
+    }
+    phase_ms = {k: max_over_ranks(float(np.mean(v))) for k, v in phases.items()}
+    flags = _native.device_errors(clear=True)
+    if flags:
+        raise RuntimeError(f"device error flags {flags:#x} during the bench")
+    clock_info = clocks.stop() if clocks else None
+
+    ms_per_step = ms / args.steps
+    value = args.batch / (ms_per_step / 1e3)
+
+    # ---- roofline: algorithmic bytes of the dominant phase -----------------
+    peak, peak_src = hbm_peak()
+    a_fwd = nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4 + C * 4
+    a_apply = nnz_rank * C * 4 + nnz_rank * 4 + (2 * T + 1) * 4 + T * C * 4 + 2 * b_rank * C * 4 + C * 4
+    a_step_survey = (nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4) + \
+                    (nnz_rank * C * 4 + 2 * b_rank * K * 4 + T * C * 4)
+    if phase_ms["forward"] >= phase_ms["backward_apply"]:
+        kname, a_bytes, t_ms = "ft_forward_kernel (forward pair: 2 launches)", a_fwd, phase_ms["forward"]
+    else:
+        kname, a_bytes, t_ms = ("backward apply (ft_segsum_kernel x2 + heavy + column sum)", a_apply,
+                                phase_ms["backward_apply"])
+    achieved = a_bytes / (t_ms / 1e3) / 1e9
+    roofline = {
+        "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+        "traffic": None, "kernel": kname, "algorithmic_bytes": a_bytes, "peak_source": f"{peak_src} hbm_gbs",
+        "step_frac": a_step_survey / (ms_per_step / 1e3) / 1e9 / peak,
+    }
+
+    # ---- e2e through the reference-facing autograd API, host buffers -------
+    e2e = None
+    if not args.no_e2e:
+        h0 = torch.from_numpy(white).pin_memory()
+        h1 = torch.from_numpy(black).pin_memory()
+        host_out = torch.empty(C, dtype=torch.float32).pin_memory()
+        Wp = W.detach().clone().requires_grad_()
+        bp = bias.detach().clone().requires_grad_()
+
+        def e2e_step():
+            d0 = h0.to(dev, non_blocking=True)
+            d1 = h1.to(dev, non_blocking=True)
+            o0, o1 = SparseLinearPairFunction.apply(d0, d1, Wp, bp)
+            torch.autograd.backward([o0, o1], [g0, g1])
+            if world > 1:
+                dist.all_reduce(Wp.grad)
+                dist.all_reduce(bp.grad)
+                Wp.grad.div_(world)
+                bp.grad.div_(world)
+            host_out.copy_(bp.grad, non_blocking=True)
+            Wp.grad = None
+            bp.grad = None
+
+        for _ in range(max(args.warmup, 3)):
+            e2e_step()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e2.record()
+        barrier()
+        ms_e2e = max_over_ranks(s2.elapsed_time(e2)) / args.steps
+        e2e = {"value": args.batch / (ms_e2e / 1e3), "unit": "positions/s",
+               "h2d_bytes_per_step": int(h0.numel() * 4 + h1.numel() * 4), "d2h_bytes_per_step": C * 4,
+               "ms_per_step": ms_e2e,
+               "path": "SparseLinearPairFunction autograd fwd+bwd, idx copied from pinned host memory, "
+                       "bias grad read back"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(white, black, W.cpu().numpy(), args.seed, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "positions/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": DATA,
+            "config": base_config(args, world, b_rank, T, K, int(nnz_rank)),
+            "phases_ms": phase_ms,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "gpu_launches_per_step": launches / max(args.steps, 1),
+            "clocks": clock_info,
+            "gpu": torch.cuda.get_device_name(dev),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,174 @@
+/*
+ * nnue_ft.h -- C ABI of the B200 (sm_100a) sparse NNUE feature transformer.
+ *
+ * Drop-in boundary for the one hot path of rgodha24/stockfish-trainer: the
+ * feature transformer behind SparseLinearFunction
+ * (src/model/modules/feature_transformer/functions.py:10-72) and its kernel
+ * factories (src/model/modules/feature_transformer/kernel.py:301-319).
+ *
+ * Conventions
+ *   - All tensors are dense, row-major, caller-owned DEVICE memory on the
+ *     current CUDA device; nothing here allocates device memory.  Scratch for
+ *     the backward comes from a caller workspace sized by
+ *     nnue_ft_backward_workspace_size().
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls only
+ *     enqueue work; none synchronises the host, so every call can be captured
+ *     in a CUDA graph.
+ *   - Feature indices are int32, -1 = empty slot, anywhere in the row.  An
+ *     index < -1 or >= num_inputs is skipped (never dereferenced) and raises a
+ *     sticky device flag read by nnue_ft_device_errors().
+ *   - Return value: NNUE_OK or a negative NNUE_ERR_* code; no exceptions
+ *     cross this boundary.  nnue_ft_last_error() describes the last failure
+ *     on the calling thread.
+ *   - Floating point: fp32 only.  The forward and the weight gradient add in
+ *     the reference's order (ascending k per position; ascending position per
+ *     feature), so both are bit-identical to the reference kernels.
+ */
+#ifndef NNUE_FT_H
+#define NNUE_FT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NNUE_OK 0
+#define NNUE_ERR_INVALID_ARGUMENT (-1)   /* null pointer, bad shape, misaligned */
+#define NNUE_ERR_UNSUPPORTED (-2)        /* sizes beyond the documented limits */
+#define NNUE_ERR_WORKSPACE (-3)          /* workspace null or too small */
+#define NNUE_ERR_CUDA (-4)               /* a CUDA launch or runtime call failed */
+
+/* Device error flags (nnue_ft_device_errors). */
+#define NNUE_DEVERR_BAD_INDEX 1u         /* index < -1 or >= num_inputs was skipped */
+#define NNUE_DEVERR_BAD_QUANT_INDEX 2u   /* quantised forward: index outside the table */
+#define NNUE_DEVERR_BAD_SEGMENT 4u       /* backward: corrupt workspace (position out of range) */
+
+/* ABI version (major * 100 + minor). */
+int nnue_ft_version(void);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices, all threads); lets a caller count launches inside a region. */
+uint64_t nnue_ft_launch_count(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char *nnue_ft_last_error(void);
+
+/* Reads (and with clear != 0 resets) the sticky device error flags of the
+ * current device.  Synchronises the device: a debugging aid, not for the
+ * hot loop. */
+int nnue_ft_device_errors(uint32_t *flags, int clear);
+
+/* Tuning knobs (names: "fwd_chunk_vec", "fwd_items_per_warp", "bwd_chunk_vec",
+ * "heavy_threshold", "heavy_cap", "sort_tile_raw", "sort_tile", "colsum_parts").
+ * Process-wide; change them only while no call is in flight and never between
+ * a backward_prepare and its backward_apply. */
+int nnue_ft_set_param(const char *name, int64_t value);
+int64_t nnue_ft_get_param(const char *name);
+
+/* ---- forward ------------------------------------------------------------
+ * Replaces the TileLang forward kernel (kernel.py:66-105) as called from
+ * SparseLinearFunction.forward (functions.py:12-48) and the factory
+ * make_sparse_input_linear_forward_kernel(max_active, output_size)(idx,
+ * weight, bias, output) (kernel.py:301-312):
+ *   output[b, c] = bias[c] + sum_{k ascending, idx[b,k] != -1} weight[idx[b,k], c]
+ * idx: [batch, max_active] int32; weight: [num_inputs, output_size] fp32;
+ * bias: [output_size]; output: [batch, output_size] (written). */
+int nnue_ft_forward(const int32_t *idx, int64_t batch, int32_t max_active, const float *weight,
+                    int64_t num_inputs, int32_t output_size, const float *bias, float *output,
+                    void *stream);
+
+/* Both perspectives in one launch (the two calls of
+ * ComposedFeatureTransformer.forward, src/model/modules/features/composed.py:49-54). */
+int nnue_ft_forward_pair(const int32_t *idx0, const int32_t *idx1, int64_t batch, int32_t max_active,
+                         const float *weight, int64_t num_inputs, int32_t output_size, const float *bias,
+                         float *out0, float *out1, void *stream);
+
+/* ---- backward -----------------------------------------------------------
+ * Replaces _build_sorted_backward_inputs (kernel.py:108-138), the bias
+ * column sum (kernel.py:269) and the TileLang backward kernel
+ * (kernel.py:141-188), as reached from SparseLinearFunction.backward
+ * (functions.py:50-72) or make_sparse_input_linear_backward_kernel
+ * (kernel.py:315-319).
+ *
+ * n_persp = 1 (idx1/grad1 unused) or 2.  For every feature row f:
+ *   sum(f) = sum over perspectives q of ( sum_{b ascending, f in idx_q[b]} grad_q[b] )
+ *   accumulate == 0: weight_grad[f] = sum(f) for EVERY row (untouched rows
+ *                    get 0, so weight_grad may be uninitialised memory);
+ *                    bias_grad = column sums.
+ *   accumulate != 0: weight_grad[f] += sum(f) for touched rows only, exactly
+ *                    the reference kernel's update; bias_grad += column sums.
+ * The backward is deterministic: same inputs, same bits. */
+size_t nnue_ft_backward_workspace_size(int64_t batch, int32_t max_active, int64_t num_inputs,
+                                       int32_t output_size, int32_t n_persp);
+
+int nnue_ft_backward(const int32_t *idx0, const int32_t *idx1, int64_t batch, int32_t max_active,
+                     const float *grad0, const float *grad1, int32_t n_persp, int64_t num_inputs,
+                     int32_t output_size, float *weight_grad, float *bias_grad, int32_t accumulate,
+                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* The two phases of nnue_ft_backward.  prepare depends only on the indices
+ * (sorted position lists per feature, in the workspace); apply consumes the
+ * gradients.  Same sizes and workspace for both; prepare may run as soon as
+ * the indices are known (e.g. right after the forward). */
+int nnue_ft_backward_prepare(const int32_t *idx0, const int32_t *idx1, int64_t batch, int32_t max_active,
+                             int32_t n_persp, int64_t num_inputs, int32_t output_size, void *workspace,
+                             size_t workspace_bytes, void *stream);
+int nnue_ft_backward_apply(const float *grad0, const float *grad1, int64_t batch, int32_t max_active,
+                           int32_t n_persp, int64_t num_inputs, int32_t output_size, float *weight_grad,
+                           float *bias_grad, int32_t accumulate, void *workspace, size_t workspace_bytes,
+                           void *stream);
+
+/* ---- quantised (int16) forward ------------------------------------------
+ * The inference forward of a serialised net (the engine's accumulator
+ * refresh; the engine is not part of the reference):
+ *   acc[b, :]  = bias_q + sum weight_q[row(idx[b,k]), :]   int16, wrapping
+ *   psqt[b, :] =          sum psqt_q[row(idx[b,k]), :]     int32, wrapping
+ * row(i) = i (export-space indices) or, with map_training != 0, the HalfKA
+ * training -> export row map of halfka_v2_hm.py:100-134.
+ * weight_q: [table_rows, l1] int16 (l1 % 8 == 0); psqt_q: [table_rows, n_psqt]
+ * int32 (n_psqt % 4 == 0); all pointers 16-byte aligned. */
+int nnue_ft_quantized_forward_pair(const int32_t *idx0, const int32_t *idx1, int32_t n_persp, int64_t batch,
+                                   int32_t max_active, const int16_t *weight_q, const int32_t *psqt_q,
+                                   int64_t table_rows, int32_t l1, int32_t n_psqt, const int16_t *bias_q,
+                                   int32_t map_training, int16_t *acc0, int16_t *acc1, int32_t *psqt0,
+                                   int32_t *psqt1, void *stream);
+
+/* HalfKAv2_hm export + FT quantisation (halfka_v2_hm.py:100-134,
+ * quantize.py:83-89): weight [24576, l1 + n_psqt] fp32, virtual [768, same]
+ * (nullable) -> weight_q [22528, l1] int16 (x * w_scale, half to even),
+ * psqt_q [22528, n_psqt] int32 (x * psqt_scale). */
+int nnue_ft_halfka_export_quantize(const float *weight, const float *virtual_weight, int32_t l1, int32_t n_psqt,
+                                   float w_scale, float psqt_scale, int16_t *weight_q, int32_t *psqt_q,
+                                   void *stream);
+
+/* Elementwise fp32 -> int16 quantisation, round half to even (bias path of
+ * quantize.py:83). */
+int nnue_ft_quantize_i16(const float *x, int64_t n, float scale, int16_t *q, void *stream);
+
+/* Number of Full_Threats inputs implied by the offset table (the reference
+ * asserts 60720, feature_extraction.rs:826). */
+int nnue_threat_table_total(void);
+
+/* ---- host-side synthetic inputs (no GPU needed) --------------------------
+ * Seeded random positions: per position an independent splitmix64 stream;
+ * kings on distinct uniform squares; U{0..30} other pieces of uniform type
+ * (P, N, B, R, Q) and colour on distinct empty squares, pawns on ranks 2-7;
+ * uniform side to move.  Positions whose Full_Threats count exceeds 128 in
+ * either perspective are redrawn from the same stream.
+ * board: [count, 64] piece ids (type * 2 + colour, 12 = empty), stm: [count]. */
+int nnue_generate_positions(uint64_t seed, int64_t first, int64_t count, uint8_t *board, uint8_t *stm);
+
+/* Feature indices of the reference's feature functions
+ * (src/rust/feature_extraction.rs:213-241, 391-404, 581-739):
+ * feature_set 0 = HalfKAv2_hm (K = 32), 1 = Full_Threats (K = 128),
+ * 2 = Full_Threats+HalfKAv2_hm (K = 160).  white/black: [count, K] int32,
+ * compacted, -1 padded; counts (nullable): [count] each.  Host memory. */
+int nnue_encode_features(const uint8_t *board, int64_t count, int32_t feature_set, int32_t *white,
+                         int32_t *black, int32_t *white_count, int32_t *black_count, int32_t nthreads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NNUE_FT_H */

@@ -1,0 +1,115 @@
+// Shared device helpers for the sparse feature-transformer kernels (sm_100a).
+//
+// Everything here is compiled into ONE translation unit (nnue_ft.cu), so the
+// sticky device error word below is a single symbol per device.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nnue {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kBlock = 256;                  // threads per block for all gather kernels
+constexpr int kWarpsPerBlock = kBlock / 32;
+
+// Sticky error flags raised by kernels instead of faulting: an index outside
+// [-1, num_inputs) is skipped (never dereferenced) and reported here.
+__device__ unsigned int g_device_errors = 0;
+enum : unsigned {
+  kErrBadIndex = 1u,       // feature index < -1 or >= num_inputs
+  kErrBadQuantIndex = 2u,  // quantised forward: index outside the table / export map
+  kErrBadSegment = 4u,     // backward: a sorted position outside [0, batch) (corrupt workspace)
+};
+
+__device__ __forceinline__ void flag_error(unsigned e) { atomicOr(&g_device_errors, e); }
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Vector access policy: float4 rows (128-bit loads) when C % 4 == 0 and the
+// pointers are 16-byte aligned, scalar floats otherwise.
+template <typename VT>
+struct Vec;
+
+template <>
+struct Vec<float4> {
+  static constexpr int kFloats = 4;
+  static __device__ __forceinline__ float4 zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  static __device__ __forceinline__ void add(float4& a, const float4& b) {
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+  }
+  static __device__ __forceinline__ float4 ldg(const float4* p) { return __ldg(p); }
+  static __device__ __forceinline__ void st_stream(float4* p, const float4& v) { __stcs(p, v); }
+};
+
+template <>
+struct Vec<float> {
+  static constexpr int kFloats = 1;
+  static __device__ __forceinline__ float zero() { return 0.f; }
+  static __device__ __forceinline__ void add(float& a, const float& b) { a += b; }
+  static __device__ __forceinline__ float ldg(const float* p) { return __ldg(p); }
+  static __device__ __forceinline__ void st_stream(float* p, const float& v) { __stcs(p, v); }
+};
+
+// Column chunking of one table row of n_vec vectors.  Chunk c covers vectors
+// [c * chunk_vec, c * chunk_vec + width(c)); the last chunk absorbs the
+// remainder.  Chunks are the OUTER grid dimension, so at any moment the
+// running blocks touch one column slice of the table / gradient -- a slice
+// sized to stay resident in L2 while it is re-read.
+struct Geom {
+  int32_t n_vec;
+  int32_t chunk_vec;
+  int32_t n_chunks;
+  int32_t last_vec;
+  __host__ __device__ __forceinline__ int begin(int c) const { return c * chunk_vec; }
+  __host__ __device__ __forceinline__ int width(int c) const {
+    return c == n_chunks - 1 ? last_vec : chunk_vec;
+  }
+};
+
+// Warp / block reductions and scans on int32.
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+__device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int t = __shfl_up_sync(kFull, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+// Inclusive scan over the whole block (blockDim.x a multiple of 32, <= 1024).
+// `scratch` must hold 33 ints.  Contains __syncthreads.
+__device__ __forceinline__ int block_inclusive_scan(int v, int* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  int incl = warp_inclusive_scan(v, lane);
+  if (lane == 31) scratch[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < nwarps ? scratch[lane] : 0;
+    t = warp_inclusive_scan(t, lane);
+    scratch[lane] = t;  // inclusive warp totals
+  }
+  __syncthreads();
+  if (warp > 0) incl += scratch[warp - 1];
+  const int total = scratch[nwarps - 1];
+  __syncthreads();
+  if (threadIdx.x == 0) scratch[32] = total;
+  __syncthreads();
+  return incl;
+}
+
+}  // namespace nnue

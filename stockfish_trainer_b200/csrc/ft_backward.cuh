@@ -1,0 +1,558 @@
+// Sparse feature-transformer BACKWARD (sm_100a).
+//
+// Reference semantics (src/model/modules/feature_transformer/kernel.py):
+//   prep  :108-138  flatten idx, drop -1, STABLE sort by feature -> for every
+//                   feature f the list of positions b that use it, ascending b
+//   kernel:167-186  acc = 0; for b in that list: acc += dOut[b];
+//                   weight_grad[f] = weight_grad[f] + acc
+//   bias  :269      bias_grad += dOut.sum(0)
+// The module-level caller (src/model/modules/features/composed.py:49-54)
+// runs this once per perspective on one shared table; autograd then adds the
+// two dense gradients.  The pair path here produces that sum directly:
+//   dW[f] = acc_white(f) + acc_black(f)
+// with each acc summed in ascending b, which is bit-identical to the
+// reference's two zero-initialised gradients added once.
+//
+// Pipeline (no host synchronisation anywhere, so it is graph-capturable):
+//   1. key = f * P + perspective.  A least-significant-digit radix sort of the
+//      (key, b) pairs, <= 10-bit digits.  Each digit pass is
+//        hist    : per warp tile, digit histogram  -> tile_hist[digit][tile]
+//        scan    : exclusive scan of tile_hist (digit-major) -> tile offsets
+//        scatter : each warp re-walks its tile in order; __match_any_sync
+//                  ranks equal digits within 32 lanes, a per-warp running
+//                  count in shared memory carries the rank across rounds.
+//      Tiles are walked in input order, so every pass is stable and the
+//      result is ordered by key with ties in original (ascending b) order.
+//      The first pass reads the raw [B, K] index arrays directly and also
+//      builds the full per-key histogram (-> segment offsets seg_start).
+//   2. classify: rows with more than `heavy_threshold` entries go to a heavy
+//      list (bounded); their work is split finer and scheduled first.
+//   3. segsum: one warp per (row, column chunk); heavy rows one warp per
+//      (row, 32-vector piece).  Every row of dW is written exactly once
+//      (rows no position touches get 0), which replaces torch.zeros + RMW.
+//   4. bias: deterministic column sum (per-part partials, fixed-order combine).
+#pragma once
+
+#include "common.cuh"
+
+namespace nnue {
+
+// ----------------------------------------------------------------------------
+// Exclusive scan (int32), reduce-then-scan in three launches.  The length is
+// either host-known or derived on the device from a count (so passes after the
+// first can size themselves from the number of valid entries without a sync).
+// ----------------------------------------------------------------------------
+struct ScanLen {
+  int64_t n;            // host length when `count` is null
+  const int32_t* count; // device entry count -> length = bins * ceil(count / tile)
+  int32_t tile;
+  int32_t bins;
+};
+
+__device__ __forceinline__ int64_t scan_length(const ScanLen& L) {
+  if (!L.count) return L.n;
+  const int64_t tiles = ((int64_t)*L.count + L.tile - 1) / L.tile;
+  return tiles * L.bins;
+}
+
+constexpr int kScanItems = 16;
+constexpr int kScanTile = kBlock * kScanItems;
+
+__global__ void __launch_bounds__(kBlock) scan_reduce_kernel(const int32_t* __restrict__ in, ScanLen L,
+                                                             int32_t* __restrict__ block_sums) {
+  __shared__ int red[32];
+  const int64_t n = scan_length(L);
+  const int64_t base = (int64_t)blockIdx.x * kScanTile;
+  int s = 0;
+  if (base < n) {
+#pragma unroll
+    for (int i = 0; i < kScanItems; ++i) {
+      const int64_t j = base + i * kBlock + threadIdx.x;
+      if (j < n) s += in[j];
+    }
+  }
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int t = threadIdx.x < kWarpsPerBlock ? red[threadIdx.x] : 0;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) block_sums[blockIdx.x] = t;
+  }
+}
+
+// Single block: exclusive scan of nb block sums, in place.
+__global__ void __launch_bounds__(1024) scan_top_kernel(int32_t* __restrict__ block_sums, int64_t nb) {
+  __shared__ int scratch[33];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int64_t base = 0; base < nb; base += blockDim.x) {
+    const int64_t j = base + threadIdx.x;
+    const int v = j < nb ? block_sums[j] : 0;
+    const int incl = block_inclusive_scan(v, scratch);
+    const int c = carry;
+    if (j < nb) block_sums[j] = c + incl - v;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = c + incl;
+    __syncthreads();
+  }
+}
+
+// out[i] = block offset + exclusive prefix inside the block.  In place is fine.
+__global__ void __launch_bounds__(kBlock) scan_down_kernel(const int32_t* in, int32_t* out, ScanLen L,
+                                                           const int32_t* __restrict__ block_sums) {
+  __shared__ int scratch[33];
+  const int64_t n = scan_length(L);
+  const int64_t base = (int64_t)blockIdx.x * kScanTile;
+  if (base >= n) return;  // uniform per block
+  const int64_t t0 = base + (int64_t)threadIdx.x * kScanItems;
+  int v[kScanItems];
+  int tsum = 0;
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    v[i] = t0 + i < n ? in[t0 + i] : 0;
+    tsum += v[i];
+  }
+  const int incl = block_inclusive_scan(tsum, scratch);
+  int run = block_sums[blockIdx.x] + incl - tsum;
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    if (t0 + i < n) out[t0 + i] = run;
+    run += v[i];
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Radix passes
+// ----------------------------------------------------------------------------
+struct RawSrc {
+  const int32_t* idx[2];  // [B, K] per perspective
+  int64_t n_raw;          // B * K
+  int32_t K;
+  int32_t T;
+  int32_t P;
+};
+
+struct PassParams {
+  RawSrc raw;                // first pass: read the raw index arrays
+  const int32_t* in_keys;    // later passes
+  const int32_t* in_vals;
+  const int32_t* count;      // later passes: device count of valid entries
+  int64_t n_src;             // first pass: P * B * K
+  int32_t tile;              // entries per warp tile, multiple of 32 * kSortBatch
+  int32_t shift;             // digit = (key >> shift) & (bins - 1)
+  int32_t bits;
+  int32_t* tile_hist;        // [bins][n_tiles]
+  int32_t* key_count;        // first pass: full histogram over keys (may be null)
+  int32_t* out_keys;         // null on the last pass
+  int32_t* out_vals;
+  int64_t out_cap;           // capacity of out_keys / out_vals
+};
+
+constexpr int kSortBatch = 16;  // rounds of 32 entries loaded before they are processed
+
+__device__ __forceinline__ void raw_entry(const RawSrc& s, int64_t e, int& key, int& b, bool& valid) {
+  const int persp = e >= s.n_raw ? 1 : 0;
+  const int r = (int)(e - (int64_t)persp * s.n_raw);
+  const int f = __ldcs((persp ? s.idx[1] : s.idx[0]) + r);
+  valid = (unsigned)f < (unsigned)s.T;
+  if (!valid && f != -1) flag_error(kErrBadIndex);
+  key = f * s.P + persp;
+  b = r / s.K;
+}
+
+template <bool RAW>
+__device__ __forceinline__ int64_t pass_n_src(const PassParams& p) {
+  return RAW ? p.n_src : (int64_t)*p.count;
+}
+
+template <bool RAW>
+__global__ void __launch_bounds__(kBlock) sort_hist_kernel(const PassParams p) {
+  extern __shared__ int32_t sh[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bins = 1 << p.bits;
+  int32_t* h = sh + warp * bins;
+  for (int i = lane; i < bins; i += 32) h[i] = 0;
+  __syncwarp();
+  const int64_t n_src = pass_n_src<RAW>(p);
+  const int64_t n_tiles = (n_src + p.tile - 1) / p.tile;
+  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (tile >= n_tiles) return;  // whole warp
+  const int64_t e0 = tile * p.tile;
+  const int64_t e1 = e0 + p.tile < n_src ? e0 + p.tile : n_src;
+  for (int64_t base = e0; base < e1; base += 32 * kSortBatch) {
+    int key[kSortBatch];
+    bool valid[kSortBatch];
+#pragma unroll
+    for (int r = 0; r < kSortBatch; ++r) {
+      const int64_t e = base + r * 32 + lane;
+      valid[r] = false;
+      key[r] = 0;
+      if (e < e1) {
+        if (RAW) {
+          int b;
+          raw_entry(p.raw, e, key[r], b, valid[r]);
+        } else {
+          key[r] = __ldg(p.in_keys + e);
+          valid[r] = true;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kSortBatch; ++r) {
+      if (valid[r]) {
+        atomicAdd(&h[(key[r] >> p.shift) & (bins - 1)], 1);
+        if (RAW && p.key_count) atomicAdd(&p.key_count[key[r]], 1);
+      }
+    }
+  }
+  __syncwarp();
+  for (int i = lane; i < bins; i += 32) p.tile_hist[(int64_t)i * n_tiles + tile] = h[i];
+}
+
+template <bool RAW>
+__global__ void __launch_bounds__(kBlock) sort_scatter_kernel(const PassParams p) {
+  extern __shared__ int32_t sh[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bins = 1 << p.bits;
+  int32_t* h = sh + warp * bins;  // running destination per digit
+  const int64_t n_src = pass_n_src<RAW>(p);
+  const int64_t n_tiles = (n_src + p.tile - 1) / p.tile;
+  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (tile >= n_tiles) return;
+  // tile_hist now holds the scanned offsets: start of (digit, tile).
+  for (int i = lane; i < bins; i += 32) h[i] = p.tile_hist[(int64_t)i * n_tiles + tile];
+  __syncwarp();
+  const int64_t e0 = tile * p.tile;
+  const int64_t e1 = e0 + p.tile < n_src ? e0 + p.tile : n_src;
+  const unsigned lt = lanemask_lt();
+  for (int64_t base = e0; base < e1; base += 32 * kSortBatch) {
+    int key[kSortBatch], val[kSortBatch];
+    bool valid[kSortBatch];
+#pragma unroll
+    for (int r = 0; r < kSortBatch; ++r) {
+      const int64_t e = base + r * 32 + lane;
+      valid[r] = false;
+      key[r] = 0;
+      val[r] = 0;
+      if (e < e1) {
+        if (RAW) {
+          raw_entry(p.raw, e, key[r], val[r], valid[r]);
+        } else {
+          key[r] = __ldg(p.in_keys + e);
+          val[r] = __ldg(p.in_vals + e);
+          valid[r] = true;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kSortBatch; ++r) {
+      const int digit = valid[r] ? ((key[r] >> p.shift) & (bins - 1)) : bins;  // `bins` = no digit
+      const unsigned peers = __match_any_sync(kFull, digit);
+      const int rank = __popc(peers & lt);
+      const int dst0 = valid[r] ? h[digit] : 0;
+      __syncwarp();
+      if (valid[r]) {
+        const int dst = dst0 + rank;
+        if ((unsigned long long)(unsigned)dst < (unsigned long long)p.out_cap) {
+          if (p.out_keys) p.out_keys[dst] = key[r];
+          p.out_vals[dst] = val[r];
+        } else {
+          flag_error(kErrBadSegment);
+        }
+        if (rank == 0) h[digit] = dst0 + __popc(peers);
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// Rows with more than `threshold` entries (both perspectives) are heavy.
+__global__ void classify_rows_kernel(const int32_t* __restrict__ seg_start, int32_t T, int32_t P,
+                                     int32_t threshold, int32_t cap, int32_t* __restrict__ n_heavy,
+                                     int32_t* __restrict__ heavy_list, uint8_t* __restrict__ row_kind) {
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= T) return;
+  const int n = seg_start[(f + 1) * P] - seg_start[f * P];
+  uint8_t kind = 0;
+  if (n > threshold) {
+    const int s = atomicAdd(n_heavy, 1);
+    if (s < cap) {
+      heavy_list[s] = (int32_t)f;
+      kind = 1;
+    }
+  }
+  row_kind[f] = kind;
+}
+
+// ----------------------------------------------------------------------------
+// Segment sums
+// ----------------------------------------------------------------------------
+struct SegParams {
+  const float* dout[2];       // [B, C] per perspective
+  const int32_t* sorted_b;    // positions, grouped by key, ascending b within a key
+  const int32_t* seg_start;   // [T * P + 1]
+  const int32_t* heavy_list;
+  const int32_t* n_heavy;
+  const uint8_t* row_kind;
+  float* dW;                  // [T, C]
+  int64_t B;                  // positions: every sorted value must lie in [0, B)
+  int32_t T;
+  int32_t P;
+  int32_t accumulate;         // 0: dW[f] = sum (all rows written); 1: dW[f] += sum (touched rows)
+  int32_t heavy_cap;
+  int32_t chunk0;             // first column chunk of this launch (blockIdx.y offset)
+  Geom g;
+};
+
+// acc[v] += dOut[b, cols] for every b in sorted_b[s, e), ascending.
+// Sorted values outside [0, B) would mean a corrupted workspace; they are
+// skipped and flagged rather than dereferenced.
+template <typename VT, int V, int U>
+__device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src, int64_t row_vec,
+                                        const int32_t* __restrict__ sb, int s, int e, int64_t B,
+                                        const bool (&ok)[V], int lane) {
+  using Ops = Vec<VT>;
+  for (int j0 = s; j0 < e; j0 += 32) {
+    const int cnt = e - j0 < 32 ? e - j0 : 32;
+    int my = lane < cnt ? __ldg(sb + j0 + lane) : 0;
+    if ((unsigned long long)(unsigned)my >= (unsigned long long)B) {
+      flag_error(kErrBadSegment);
+      my = -1;
+    }
+    for (int u0 = 0; u0 < cnt; u0 += U) {
+      int rows[U];
+      bool has[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        rows[u] = __shfl_sync(kFull, my, (u0 + u) & 31);
+        has[u] = u0 + u < cnt && rows[u] >= 0;
+      }
+      VT w[U][V];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (has[u] && ok[v]) w[u][v] = Ops::ldg(src + (int64_t)rows[u] * row_vec + 32 * v);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (has[u] && ok[v]) Ops::add(acc[v], w[u][v]);
+    }
+  }
+}
+
+template <typename VT, int V>
+__device__ __forceinline__ void seg_write(const SegParams& p, int64_t f, int col, const VT (&tot)[V],
+                                          const bool (&ok)[V]) {
+  using Ops = Vec<VT>;
+  VT* dst = reinterpret_cast<VT*>(p.dW) + f * (int64_t)p.g.n_vec + col;
+  if (p.accumulate) {
+    const bool touched = p.seg_start[(f + 1) * p.P] > p.seg_start[f * p.P];
+    if (!touched) return;
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+      if (ok[v]) {
+        VT cur = dst[32 * v];
+        Ops::add(cur, tot[v]);
+        dst[32 * v] = cur;
+      }
+  } else {
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+      if (ok[v]) dst[32 * v] = tot[v];
+  }
+}
+
+// Light rows: one warp per (row, column chunk), V vectors per lane, U rows of
+// dOut in flight.  Heavy rows are skipped here (ft_segsum_heavy_kernel).
+template <typename VT, int V, int U>
+__global__ void __launch_bounds__(kBlock) ft_segsum_kernel(const SegParams p) {
+  using Ops = Vec<VT>;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int chunk = p.chunk0 + blockIdx.y;
+  const int c0 = p.g.begin(chunk);
+  const int width = p.g.width(chunk);
+  const int64_t row_vec = p.g.n_vec;
+  const int64_t f = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (f >= p.T) return;
+  if (p.row_kind[f]) return;
+  bool ok[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) ok[v] = lane + 32 * v < width;
+  VT tot[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) tot[v] = Ops::zero();
+  for (int q = 0; q < p.P; ++q) {
+    VT acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = Ops::zero();
+    const int s = p.seg_start[f * p.P + q], e = p.seg_start[f * p.P + q + 1];
+    const VT* src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]) + c0 + lane;
+    seg_sum<VT, V, U>(acc, src, row_vec, p.sorted_b, s, e, p.B, ok, lane);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if (q == 0) tot[v] = acc[v];
+      else Ops::add(tot[v], acc[v]);
+    }
+  }
+  seg_write<VT, V>(p, f, c0 + lane, tot, ok);
+}
+
+// ---------------------------------------------------------------------------
+// Heavy rows.  A row that thousands of positions share is a long serial sum
+// per column (the reference order is ascending b, which the result must keep),
+// so the only parallelism is across columns.  Each warp owns one 32-vector
+// piece of a column chunk and streams the dOut rows through a private
+// shared-memory ring with cp.async: every lane copies its own 16 bytes of
+// entry j into slot j % kHeavyStages and later reads back only what it
+// copied, so no barrier is needed and kHeavyStages entries stay in flight
+// per warp without holding registers.
+// ---------------------------------------------------------------------------
+constexpr int kHeavyWarps = 2;
+constexpr int kHeavyStages = 48;
+
+template <typename VT>
+__device__ __forceinline__ void cp_async_vec(VT* smem_dst, const VT* gsrc, bool pred);
+
+template <>
+__device__ __forceinline__ void cp_async_vec<float4>(float4* smem_dst, const float4* gsrc, bool pred) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+  const int n = pred ? 16 : 0;  // 0 source bytes: zero-fill, source not read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gsrc), "r"(n) : "memory");
+}
+
+template <>
+__device__ __forceinline__ void cp_async_vec<float>(float* smem_dst, const float* gsrc, bool pred) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+  const int n = pred ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(gsrc), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <typename VT>
+__global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const SegParams p) {
+  using Ops = Vec<VT>;
+  extern __shared__ __align__(16) unsigned char heavy_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  VT* ring = reinterpret_cast<VT*>(heavy_smem) + warp * kHeavyStages * 32 + lane;
+  const int chunk = p.chunk0 + blockIdx.y;
+  const int c0 = p.g.begin(chunk);
+  const int width = p.g.width(chunk);
+  const int pieces = (width + 31) / 32;
+  const int wi = blockIdx.x * kHeavyWarps + warp;
+  const int slot = wi / pieces, piece = wi - slot * pieces;
+  const int nh = *p.n_heavy < p.heavy_cap ? *p.n_heavy : p.heavy_cap;
+  if (slot >= nh) return;
+  const int64_t f = p.heavy_list[slot];
+  const int col = c0 + piece * 32 + lane;
+  const bool ok1 = piece * 32 + lane < width;
+  const int64_t row_vec = p.g.n_vec;
+
+  VT tot = Ops::zero();
+  for (int q = 0; q < p.P; ++q) {
+    const int s = p.seg_start[f * p.P + q], e = p.seg_start[f * p.P + q + 1];
+    const VT* src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]) + (ok1 ? col : 0);
+    VT acc = Ops::zero();
+    // issue pointer t runs kHeavyStages entries ahead of the consume pointer j
+    int t = s;
+    int idx_base = -1, my_b = 0;
+    auto issue = [&](int slot_i) {
+      if (t < e) {
+        const int base = t & ~31;
+        if (base != idx_base) {
+          idx_base = base;
+          my_b = base + lane < e ? __ldg(p.sorted_b + base + lane) : 0;
+        }
+        const int b = __shfl_sync(kFull, my_b, t & 31);
+        const bool in_range = (unsigned long long)(unsigned)b < (unsigned long long)p.B;
+        if (!in_range) flag_error(kErrBadSegment);
+        cp_async_vec<VT>(ring + slot_i * 32, src + (in_range ? (int64_t)b * row_vec : 0), ok1 && in_range);
+      }
+      cp_async_commit();  // empty groups keep the pending count constant
+      ++t;
+    };
+    for (int i = 0; i < kHeavyStages; ++i) issue(i);
+    for (int j = s, stage = 0; j < e; ++j) {
+      cp_async_wait<kHeavyStages - 1>();
+      Ops::add(acc, ring[stage * 32]);
+      __syncwarp();
+      issue(stage);
+      stage = stage + 1 == kHeavyStages ? 0 : stage + 1;
+    }
+    cp_async_wait<0>();
+    if (q == 0) tot = acc;
+    else Ops::add(tot, acc);
+  }
+  const bool ok[1] = {ok1};
+  const VT t1[1] = {tot};
+  seg_write<VT, 1>(p, f, col, t1, ok);
+}
+
+// ----------------------------------------------------------------------------
+// Bias gradient: deterministic column sum over positions, both perspectives.
+// ----------------------------------------------------------------------------
+struct ColParams {
+  const float* dout[2];
+  int64_t B;
+  int32_t P;
+  int32_t n_vec;
+  int32_t parts;
+  float* partial;  // [P][parts][n_vec] vectors
+};
+
+template <typename VT>
+__global__ void __launch_bounds__(kBlock) colsum_partial_kernel(const ColParams p) {
+  using Ops = Vec<VT>;
+  const int part = blockIdx.x, q = blockIdx.y;
+  const int64_t r0 = p.B * part / p.parts, r1 = p.B * (part + 1) / p.parts;
+  const VT* __restrict__ src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]);
+  VT* dst = reinterpret_cast<VT*>(p.partial) + ((int64_t)q * p.parts + part) * p.n_vec;
+  for (int col = threadIdx.x; col < p.n_vec; col += blockDim.x) {
+    VT acc = Ops::zero();
+    int64_t r = r0;
+    for (; r + 8 <= r1; r += 8) {
+      VT t[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[i] = Ops::ldg(src + (r + i) * p.n_vec + col);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) Ops::add(acc, t[i]);
+    }
+    for (; r < r1; ++r) Ops::add(acc, Ops::ldg(src + r * p.n_vec + col));
+    dst[col] = acc;
+  }
+}
+
+template <typename VT>
+__global__ void colsum_final_kernel(const float* __restrict__ partial, int32_t P, int32_t parts, int32_t n_vec,
+                                    float* dB, int32_t accumulate) {
+  using Ops = Vec<VT>;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= n_vec) return;
+  const VT* src = reinterpret_cast<const VT*>(partial);
+  VT tot = Ops::zero();
+  for (int q = 0; q < P; ++q) {
+    VT s = Ops::zero();
+    for (int i = 0; i < parts; ++i) Ops::add(s, src[((int64_t)q * parts + i) * n_vec + col]);
+    if (q == 0) tot = s;
+    else Ops::add(tot, s);
+  }
+  VT* d = reinterpret_cast<VT*>(dB) + col;
+  if (accumulate) {
+    VT cur = *d;
+    Ops::add(cur, tot);
+    *d = cur;
+  } else {
+    *d = tot;
+  }
+}
+
+}  // namespace nnue

@@ -1,0 +1,676 @@
+// C ABI of the sparse NNUE feature transformer for B200 (sm_100a).
+// Declarations and contracts: include/nnue_ft.h.
+//
+// One translation unit: the kernels live in the *.cuh files included here.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/nnue_ft.h"
+#include "common.cuh"
+#include "ft_backward.cuh"
+#include "ft_forward.cuh"
+#include "ft_quant.cuh"
+
+namespace nnue {
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<unsigned long long> g_launches{0};  // kernel launches issued by this library
+
+inline void count_launch(unsigned n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(NNUE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return NNUE_OK;
+}
+
+struct Tuning {
+  int64_t fwd_chunk_vec = 64;      // forward column chunk, in 16-byte vectors
+  int64_t fwd_items_per_warp = 4;  // (perspective, position) items per warp
+  int64_t bwd_chunk_vec = 64;      // backward column chunk, in 16-byte vectors
+  int64_t heavy_threshold = 256;   // rows with more entries are split finer
+  int64_t heavy_cap = 512;         // at most this many heavy rows per call
+  int64_t sort_tile_raw = 2048;    // raw index entries per warp in the first sort pass
+  int64_t sort_tile = 1024;        // entries per warp in later sort passes
+  int64_t colsum_parts = 296;      // position ranges of the bias column sum
+};
+Tuning g_tune;
+
+struct ParamRef {
+  const char* name;
+  int64_t* field;
+  int64_t lo, hi;
+};
+
+ParamRef* params() {
+  static ParamRef p[] = {
+      {"fwd_chunk_vec", &g_tune.fwd_chunk_vec, 0, 1 << 20},
+      {"fwd_items_per_warp", &g_tune.fwd_items_per_warp, 1, 1024},
+      {"bwd_chunk_vec", &g_tune.bwd_chunk_vec, 0, 1 << 20},
+      {"heavy_threshold", &g_tune.heavy_threshold, 1, int64_t(1) << 40},
+      {"heavy_cap", &g_tune.heavy_cap, 0, 1 << 24},
+      {"sort_tile_raw", &g_tune.sort_tile_raw, 32 * kSortBatch, 1 << 20},
+      {"sort_tile", &g_tune.sort_tile, 32 * kSortBatch, 1 << 20},
+      {"colsum_parts", &g_tune.colsum_parts, 1, 1 << 16},
+      {nullptr, nullptr, 0, 0},
+  };
+  return p;
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Column geometry.  `chunk` <= 0 or >= n_vec: one chunk.  Otherwise chunks of
+// `chunk` vectors with the remainder folded into the last one.  Chunks are
+// kept >= 8 vectors so the grid's y extent stays small.
+Geom make_geom(int32_t n_vec, int64_t chunk) {
+  Geom g;
+  g.n_vec = n_vec;
+  if (chunk <= 0 || chunk >= n_vec) {
+    g.chunk_vec = n_vec;
+    g.n_chunks = 1;
+    g.last_vec = n_vec;
+    return g;
+  }
+  chunk = std::max<int64_t>(chunk, 8);
+  g.chunk_vec = (int32_t)chunk;
+  g.n_chunks = (int32_t)std::max<int64_t>(1, n_vec / chunk);
+  g.last_vec = n_vec - (g.n_chunks - 1) * g.chunk_vec;
+  return g;
+}
+
+int lanes_per_row(const Geom& g) {  // vectors per lane needed by the widest chunk
+  const int w = std::max(g.n_chunks > 1 ? g.chunk_vec : 0, g.last_vec);
+  return (w + 31) / 32;
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+template <typename VT, int V>
+void launch_forward_v(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
+  constexpr int U = V <= 4 ? 4 : 2;
+  const int64_t n_items = (int64_t)p.P * p.B;
+  const int64_t warps = ceil_div(n_items, p.items_per_warp);
+  p.chunk0 = chunk0;
+  dim3 grid((unsigned)ceil_div(warps, kWarpsPerBlock), (unsigned)n_chunks);
+  count_launch();
+  ft_forward_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
+}
+
+template <typename VT>
+void launch_forward_range(const FwdParams& p, int chunk0, int n_chunks, int width, cudaStream_t s) {
+  switch ((width + 31) / 32) {
+    case 1: launch_forward_v<VT, 1>(p, chunk0, n_chunks, s); break;
+    case 2: launch_forward_v<VT, 2>(p, chunk0, n_chunks, s); break;
+    case 3: launch_forward_v<VT, 3>(p, chunk0, n_chunks, s); break;
+    case 4: launch_forward_v<VT, 4>(p, chunk0, n_chunks, s); break;
+    default: launch_forward_v<VT, 8>(p, chunk0, n_chunks, s); break;
+  }
+}
+
+// Chunks [0, n-1) share one width; the last (wider) chunk gets its own launch
+// so each launch is compiled for exactly the vectors per lane it needs.
+template <typename VT>
+void launch_forward(const FwdParams& p, cudaStream_t s) {
+  if (p.g.n_chunks > 1) launch_forward_range<VT>(p, 0, p.g.n_chunks - 1, p.g.chunk_vec, s);
+  launch_forward_range<VT>(p, p.g.n_chunks - 1, 1, p.g.last_vec, s);
+}
+
+int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int32_t K, const float* W,
+                 int64_t T, int32_t C, const float* bias, float* out0, float* out1, cudaStream_t s) {
+  if (B < 0 || K < 0 || T < 0 || C <= 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "forward: bad sizes");
+  if (T > INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "forward: num_inputs exceeds int32 index range");
+  if (B == 0) return NNUE_OK;
+  if (!idx0 || !out0 || !bias || (T > 0 && !W) || (P == 2 && (!idx1 || !out1)))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "forward: null pointer");
+  const bool v4 = (C % 4 == 0) && aligned16(W) && aligned16(bias) && aligned16(out0) &&
+                  (P == 1 || aligned16(out1));
+  FwdParams p{};
+  p.idx[0] = idx0;
+  p.idx[1] = P == 2 ? idx1 : idx0;
+  p.out[0] = out0;
+  p.out[1] = P == 2 ? out1 : out0;
+  p.W = W;
+  p.bias = bias;
+  p.B = B;
+  p.K = K;
+  p.T = (int32_t)T;
+  p.P = P;
+  p.items_per_warp = (int32_t)g_tune.fwd_items_per_warp;
+  if (v4) {
+    p.g = make_geom(C / 4, g_tune.fwd_chunk_vec);
+    launch_forward<float4>(p, s);
+  } else {
+    p.g = make_geom(C, g_tune.fwd_chunk_vec * 4);
+    launch_forward<float>(p, s);
+  }
+  return check_launch("forward");
+}
+
+// ---------------------------------------------------------------------------
+// backward plan: workspace layout shared by prepare / apply / size query
+// ---------------------------------------------------------------------------
+struct BwdPlan {
+  int64_t B = 0, T = 0, NK = 0, nnz_max = 0;
+  int32_t K = 0, C = 0, P = 0;
+  int bits = 0, npass = 0;
+  int dbits[3] = {0, 0, 0}, shift[3] = {0, 0, 0};
+  int64_t tile_raw = 0, tile = 0, tiles_raw = 0, tiles_max = 0, hist_len = 0, scan_blocks = 0;
+  int64_t heavy_cap = 0, heavy_threshold = 0, parts = 0;
+  size_t off_seg = 0, off_hist = 0, off_bsum = 0, off_ka = 0, off_va = 0, off_kb = 0, off_vb = 0;
+  size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, total = 0;
+};
+
+int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl) {
+  if (P != 1 && P != 2) return fail(NNUE_ERR_INVALID_ARGUMENT, "backward: n_persp must be 1 or 2");
+  if (B < 0 || K < 0 || T <= 0 || C <= 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "backward: bad sizes");
+  pl.B = B;
+  pl.K = K;
+  pl.T = T;
+  pl.C = C;
+  pl.P = P;
+  pl.NK = T * P;
+  if (pl.NK >= (int64_t(1) << 30))
+    return fail(NNUE_ERR_UNSUPPORTED, "backward: num_inputs * n_persp must be < 2^30");
+  pl.nnz_max = (int64_t)P * B * K;
+  if (pl.nnz_max >= INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "backward: n_persp * batch * max_active >= 2^31");
+  int bits = 1;
+  while ((int64_t(1) << bits) < pl.NK) ++bits;
+  pl.bits = bits;
+  pl.npass = (int)ceil_div(bits, 10);
+  for (int i = 0, sh = 0; i < pl.npass; ++i) {
+    const int d = (int)ceil_div(bits - sh, pl.npass - i);
+    pl.dbits[i] = d;
+    pl.shift[i] = sh;
+    sh += d;
+  }
+  pl.tile_raw = g_tune.sort_tile_raw / (32 * kSortBatch) * (32 * kSortBatch);
+  pl.tile = g_tune.sort_tile / (32 * kSortBatch) * (32 * kSortBatch);
+  pl.tiles_raw = ceil_div(pl.nnz_max, pl.tile_raw);
+  pl.tiles_max = ceil_div(pl.nnz_max, pl.tile);
+  pl.hist_len = (int64_t(1) << pl.dbits[0]) * pl.tiles_raw;
+  for (int i = 1; i < pl.npass; ++i)
+    pl.hist_len = std::max<int64_t>(pl.hist_len, (int64_t(1) << pl.dbits[i]) * pl.tiles_max);
+  pl.scan_blocks = std::max(ceil_div(pl.hist_len, kScanTile), ceil_div(pl.NK + 1, kScanTile));
+  pl.heavy_cap = std::min<int64_t>(g_tune.heavy_cap, T);
+  pl.heavy_threshold = g_tune.heavy_threshold;
+  pl.parts = std::max<int64_t>(1, std::min<int64_t>(g_tune.colsum_parts, B));
+  const int64_t n_vec_floats = C;  // partial sums stored as floats either way
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align_up(o + std::max<size_t>(bytes, 1));
+    return at;
+  };
+  pl.off_seg = take(sizeof(int32_t) * (pl.NK + 1));
+  pl.off_hist = take(sizeof(int32_t) * pl.hist_len);
+  pl.off_bsum = take(sizeof(int32_t) * (pl.scan_blocks + 1));
+  pl.off_ka = take(sizeof(int32_t) * pl.nnz_max);
+  pl.off_va = take(sizeof(int32_t) * pl.nnz_max);
+  pl.off_kb = take(pl.npass >= 3 ? sizeof(int32_t) * pl.nnz_max : 0);
+  pl.off_vb = take(pl.npass >= 2 ? sizeof(int32_t) * pl.nnz_max : 0);
+  pl.off_nheavy = take(sizeof(int32_t));
+  pl.off_heavy = take(sizeof(int32_t) * pl.heavy_cap);
+  pl.off_kind = take(sizeof(uint8_t) * T);
+  pl.off_partial = take(sizeof(float) * P * pl.parts * n_vec_floats);
+  pl.total = o;
+  return NNUE_OK;
+}
+
+struct Ws {
+  int32_t *seg, *hist, *bsum, *ka, *va, *kb, *vb, *nheavy, *heavy;
+  uint8_t* kind;
+  float* partial;
+};
+
+Ws carve(const BwdPlan& pl, void* base) {
+  char* b = static_cast<char*>(base);
+  Ws w;
+  w.seg = reinterpret_cast<int32_t*>(b + pl.off_seg);
+  w.hist = reinterpret_cast<int32_t*>(b + pl.off_hist);
+  w.bsum = reinterpret_cast<int32_t*>(b + pl.off_bsum);
+  w.ka = reinterpret_cast<int32_t*>(b + pl.off_ka);
+  w.va = reinterpret_cast<int32_t*>(b + pl.off_va);
+  w.kb = reinterpret_cast<int32_t*>(b + pl.off_kb);
+  w.vb = reinterpret_cast<int32_t*>(b + pl.off_vb);
+  w.nheavy = reinterpret_cast<int32_t*>(b + pl.off_nheavy);
+  w.heavy = reinterpret_cast<int32_t*>(b + pl.off_heavy);
+  w.kind = reinterpret_cast<uint8_t*>(b + pl.off_kind);
+  w.partial = reinterpret_cast<float*>(b + pl.off_partial);
+  return w;
+}
+
+// sorted position list = values written by the last pass
+const int32_t* sorted_values(const BwdPlan& pl, const Ws& w) { return (pl.npass % 2 == 1) ? w.va : w.vb; }
+
+void run_scan(int32_t* data, ScanLen L, int64_t max_len, int32_t* bsum, cudaStream_t s) {
+  const int64_t nb = ceil_div(max_len, kScanTile);
+  if (nb == 0) return;
+  count_launch();
+  scan_reduce_kernel<<<(unsigned)nb, kBlock, 0, s>>>(data, L, bsum);
+  count_launch();
+  scan_top_kernel<<<1, 1024, 0, s>>>(bsum, nb);
+  count_launch();
+  scan_down_kernel<<<(unsigned)nb, kBlock, 0, s>>>(data, data, L, bsum);
+}
+
+int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, const Ws& w, cudaStream_t s) {
+  if (cudaMemsetAsync(w.seg, 0, sizeof(int32_t) * (pl.NK + 1), s) != cudaSuccess ||
+      cudaMemsetAsync(w.nheavy, 0, sizeof(int32_t), s) != cudaSuccess)
+    return check_launch("backward_prepare: memset");
+  RawSrc raw{};
+  raw.idx[0] = idx0;
+  raw.idx[1] = pl.P == 2 ? idx1 : idx0;
+  raw.n_raw = pl.B * pl.K;
+  raw.K = pl.K;
+  raw.T = (int32_t)pl.T;
+  raw.P = pl.P;
+  for (int i = 0; i < pl.npass; ++i) {
+    const bool first = i == 0, last = i == pl.npass - 1;
+    PassParams pp{};
+    pp.raw = raw;
+    pp.n_src = pl.nnz_max;
+    pp.count = w.seg + pl.NK;  // number of valid entries, known after pass 0's scan
+    pp.shift = pl.shift[i];
+    pp.bits = pl.dbits[i];
+    pp.tile = (int32_t)(first ? pl.tile_raw : pl.tile);
+    pp.tile_hist = w.hist;
+    pp.key_count = first ? w.seg : nullptr;
+    // ping-pong: pass 0 -> A, pass 1 -> B, pass 2 -> A
+    int32_t* ok_ = (i % 2 == 0) ? w.ka : w.kb;
+    int32_t* ov_ = (i % 2 == 0) ? w.va : w.vb;
+    pp.in_keys = (i % 2 == 1) ? w.ka : w.kb;
+    pp.in_vals = (i % 2 == 1) ? w.va : w.vb;
+    pp.out_keys = last ? nullptr : ok_;
+    pp.out_vals = ov_;
+    pp.out_cap = pl.nnz_max;
+    const int bins = 1 << pl.dbits[i];
+    const size_t smem = sizeof(int32_t) * bins * kWarpsPerBlock;
+    const int64_t tiles = first ? pl.tiles_raw : pl.tiles_max;
+    if (tiles == 0) continue;
+    const unsigned grid = (unsigned)ceil_div(tiles, kWarpsPerBlock);
+    if (first) {
+      count_launch();
+      sort_hist_kernel<true><<<grid, kBlock, smem, s>>>(pp);
+      run_scan(w.hist, ScanLen{bins * tiles, nullptr, 0, 0}, bins * tiles, w.bsum, s);
+      run_scan(w.seg, ScanLen{pl.NK + 1, nullptr, 0, 0}, pl.NK + 1, w.bsum, s);
+      count_launch();
+      sort_scatter_kernel<true><<<grid, kBlock, smem, s>>>(pp);
+    } else {
+      count_launch();
+      sort_hist_kernel<false><<<grid, kBlock, smem, s>>>(pp);
+      run_scan(w.hist, ScanLen{0, pp.count, pp.tile, bins}, (int64_t)bins * tiles, w.bsum, s);
+      count_launch();
+      sort_scatter_kernel<false><<<grid, kBlock, smem, s>>>(pp);
+    }
+  }
+  if (pl.nnz_max == 0) {
+    // no entries: seg is all zero already (memset); nothing else to do
+  }
+  count_launch();
+  classify_rows_kernel<<<(unsigned)ceil_div(pl.T, kBlock), kBlock, 0, s>>>(
+      w.seg, (int32_t)pl.T, pl.P, (int32_t)std::min<int64_t>(pl.heavy_threshold, INT32_MAX),
+      (int32_t)pl.heavy_cap, w.nheavy, w.heavy, w.kind);
+  return check_launch("backward_prepare");
+}
+
+template <typename VT, int V>
+void launch_segsum_v(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
+  constexpr int U = V <= 4 ? 4 : 2;
+  p.chunk0 = chunk0;
+  dim3 grid((unsigned)ceil_div(p.T, kWarpsPerBlock), (unsigned)n_chunks);
+  count_launch();
+  ft_segsum_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
+}
+
+template <typename VT>
+void launch_segsum_range(const SegParams& p, int chunk0, int n_chunks, int width, cudaStream_t s) {
+  switch ((width + 31) / 32) {
+    case 1: launch_segsum_v<VT, 1>(p, chunk0, n_chunks, s); break;
+    case 2: launch_segsum_v<VT, 2>(p, chunk0, n_chunks, s); break;
+    case 3: launch_segsum_v<VT, 3>(p, chunk0, n_chunks, s); break;
+    case 4: launch_segsum_v<VT, 4>(p, chunk0, n_chunks, s); break;
+    default: launch_segsum_v<VT, 8>(p, chunk0, n_chunks, s); break;
+  }
+}
+
+template <typename VT>
+void launch_segsum_light(const SegParams& p, cudaStream_t s) {
+  if (p.g.n_chunks > 1) launch_segsum_range<VT>(p, 0, p.g.n_chunks - 1, p.g.chunk_vec, s);
+  launch_segsum_range<VT>(p, p.g.n_chunks - 1, 1, p.g.last_vec, s);
+}
+
+template <typename VT>
+constexpr size_t heavy_smem_bytes() {
+  return sizeof(VT) * 32 * kHeavyStages * kHeavyWarps;
+}
+
+template <typename VT>
+int launch_segsum_heavy(SegParams p, cudaStream_t s) {
+  if (p.heavy_cap == 0) return NNUE_OK;
+  constexpr size_t smem = heavy_smem_bytes<VT>();
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(ft_segsum_heavy_kernel<VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return check_launch("backward_apply: heavy kernel shared memory");
+  const int pieces_max = lanes_per_row(p.g);
+  p.chunk0 = 0;
+  dim3 grid((unsigned)ceil_div((int64_t)p.heavy_cap * pieces_max, kHeavyWarps), (unsigned)p.g.n_chunks);
+  count_launch();
+  ft_segsum_heavy_kernel<VT><<<grid, 32 * kHeavyWarps, smem, s>>>(p);
+  return NNUE_OK;
+}
+
+// Per-device side stream + fork/join events.  Heavy rows and the bias column
+// sum run there, concurrently with the light-row kernel on the caller's
+// stream.  Created once per device and kept for the life of the process.
+struct DeviceAux {
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_aux_mu;
+DeviceAux g_aux[64];
+
+int device_aux(DeviceAux** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(NNUE_ERR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+  DeviceAux& a = g_aux[dev];
+  if (!a.side) {
+    int lo = 0, hi = 0;
+    if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
+        cudaStreamCreateWithPriority(&a.side, cudaStreamNonBlocking, hi) != cudaSuccess ||
+        cudaEventCreateWithFlags(&a.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&a.join, cudaEventDisableTiming) != cudaSuccess)
+      return check_launch("creating the side stream");
+  }
+  *out = &a;
+  return NNUE_OK;
+}
+
+template <typename VT>
+void launch_colsum(const float* g0, const float* g1, const BwdPlan& pl, int32_t n_vec, float* partial, float* dB,
+                   int32_t accumulate, cudaStream_t s) {
+  ColParams c{};
+  c.dout[0] = g0;
+  c.dout[1] = pl.P == 2 ? g1 : g0;
+  c.B = pl.B;
+  c.P = pl.P;
+  c.n_vec = n_vec;
+  c.parts = (int32_t)pl.parts;
+  c.partial = partial;
+  count_launch();
+  colsum_partial_kernel<VT><<<dim3((unsigned)pl.parts, (unsigned)pl.P), kBlock, 0, s>>>(c);
+  count_launch();
+  colsum_final_kernel<VT><<<(unsigned)ceil_div(n_vec, kBlock), kBlock, 0, s>>>(partial, pl.P, (int32_t)pl.parts,
+                                                                                n_vec, dB, accumulate);
+}
+
+int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w, float* dW, float* dB,
+               int32_t accumulate, cudaStream_t s) {
+  const bool v4 = (pl.C % 4 == 0) && aligned16(g0) && (pl.P == 1 || aligned16(g1)) && aligned16(dW) &&
+                  aligned16(dB) && aligned16(w.partial);
+  SegParams p{};
+  p.dout[0] = g0;
+  p.dout[1] = pl.P == 2 ? g1 : g0;
+  p.sorted_b = sorted_values(pl, w);
+  p.seg_start = w.seg;
+  p.heavy_list = w.heavy;
+  p.n_heavy = w.nheavy;
+  p.row_kind = w.kind;
+  p.dW = dW;
+  p.B = pl.B;
+  p.T = (int32_t)pl.T;
+  p.P = pl.P;
+  p.accumulate = accumulate ? 1 : 0;
+  p.heavy_cap = (int32_t)pl.heavy_cap;
+  p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec) : make_geom(pl.C, g_tune.bwd_chunk_vec * 4);
+
+  DeviceAux* aux = nullptr;
+  int rc = device_aux(&aux);
+  if (rc != NNUE_OK) return rc;
+  {
+    // fork: heavy rows + bias column sum on the side stream
+    std::lock_guard<std::mutex> lock(g_aux_mu);
+    if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
+      return check_launch("backward_apply: fork");
+    rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
+    if (rc != NNUE_OK) return rc;
+    if (v4) launch_colsum<float4>(g0, g1, pl, pl.C / 4, w.partial, dB, p.accumulate, aux->side);
+    else launch_colsum<float>(g0, g1, pl, pl.C, w.partial, dB, p.accumulate, aux->side);
+    if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
+  }
+  if (v4) launch_segsum_light<float4>(p, s);
+  else launch_segsum_light<float>(p, s);
+  // A later record of `join` by another call is further down the same
+  // in-order side stream, so waiting on it also covers this call's work.
+  if (cudaStreamWaitEvent(s, aux->join, 0) != cudaSuccess) return check_launch("backward_apply: join");
+  return check_launch("backward_apply");
+}
+
+int check_bwd_args(const int32_t* idx0, const int32_t* idx1, int P, void* ws, size_t ws_bytes,
+                   const BwdPlan& pl) {
+  if (!idx0 || (P == 2 && !idx1)) return fail(NNUE_ERR_INVALID_ARGUMENT, "backward: null index pointer");
+  if (!ws) return fail(NNUE_ERR_WORKSPACE, "backward: null workspace");
+  if (ws_bytes < pl.total)
+    return fail(NNUE_ERR_WORKSPACE, "backward: workspace %zu bytes < required %zu", ws_bytes, pl.total);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(NNUE_ERR_WORKSPACE, "backward: workspace not 256-byte aligned");
+  return NNUE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// quantised forward
+// ---------------------------------------------------------------------------
+template <int VQ>
+void launch_qforward_v(const QFwdParams& p, cudaStream_t s) {
+  constexpr int U = VQ <= 4 ? 4 : 2;
+  const int64_t n_items = (int64_t)p.P * p.B;
+  const int64_t warps = ceil_div(n_items, p.items_per_warp);
+  count_launch();
+  ft_qforward_kernel<VQ, U><<<(unsigned)ceil_div(warps, kWarpsPerBlock), kBlock, 0, s>>>(p);
+}
+
+}  // namespace
+}  // namespace nnue
+
+using namespace nnue;
+
+extern "C" {
+
+int nnue_ft_version(void) { return 100; }
+
+uint64_t nnue_ft_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+const char* nnue_ft_last_error(void) { return g_last_error.c_str(); }
+
+int nnue_ft_device_errors(uint32_t* flags, int clear) {
+  if (!flags) return fail(NNUE_ERR_INVALID_ARGUMENT, "device_errors: null flags");
+  if (cudaDeviceSynchronize() != cudaSuccess) return check_launch("device_errors: synchronize");
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_errors, sizeof(v)) != cudaSuccess) return check_launch("device_errors: read");
+  if (clear) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_device_errors, &zero, sizeof(zero)) != cudaSuccess)
+      return check_launch("device_errors: clear");
+  }
+  *flags = v;
+  return NNUE_OK;
+}
+
+int nnue_ft_set_param(const char* name, int64_t value) {
+  if (!name) return fail(NNUE_ERR_INVALID_ARGUMENT, "set_param: null name");
+  for (ParamRef* p = params(); p->name; ++p) {
+    if (std::strcmp(p->name, name) == 0) {
+      if (value < p->lo || value > p->hi)
+        return fail(NNUE_ERR_INVALID_ARGUMENT, "set_param: %s=%lld outside [%lld, %lld]", name, (long long)value,
+                    (long long)p->lo, (long long)p->hi);
+      *p->field = value;
+      return NNUE_OK;
+    }
+  }
+  return fail(NNUE_ERR_INVALID_ARGUMENT, "set_param: unknown parameter '%s'", name);
+}
+
+int64_t nnue_ft_get_param(const char* name) {
+  if (!name) return -1;
+  for (ParamRef* p = params(); p->name; ++p)
+    if (std::strcmp(p->name, name) == 0) return *p->field;
+  return -1;
+}
+
+int nnue_ft_forward(const int32_t* idx, int64_t batch, int32_t max_active, const float* weight, int64_t num_inputs,
+                    int32_t output_size, const float* bias, float* output, void* stream) {
+  return forward_impl(idx, nullptr, 1, batch, max_active, weight, num_inputs, output_size, bias, output, nullptr,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int nnue_ft_forward_pair(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active,
+                         const float* weight, int64_t num_inputs, int32_t output_size, const float* bias, float* out0,
+                         float* out1, void* stream) {
+  return forward_impl(idx0, idx1, 2, batch, max_active, weight, num_inputs, output_size, bias, out0, out1,
+                      static_cast<cudaStream_t>(stream));
+}
+
+size_t nnue_ft_backward_workspace_size(int64_t batch, int32_t max_active, int64_t num_inputs, int32_t output_size,
+                                       int32_t n_persp) {
+  BwdPlan pl;
+  if (make_plan(batch, max_active, num_inputs, output_size, n_persp, pl) != NNUE_OK) return 0;
+  return pl.total;
+}
+
+int nnue_ft_backward_prepare(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active,
+                             int32_t n_persp, int64_t num_inputs, int32_t output_size, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  BwdPlan pl;
+  int rc = make_plan(batch, max_active, num_inputs, output_size, n_persp, pl);
+  if (rc != NNUE_OK) return rc;
+  rc = check_bwd_args(idx0, idx1, n_persp, workspace, workspace_bytes, pl);
+  if (rc != NNUE_OK) return rc;
+  return prepare_impl(idx0, idx1, pl, carve(pl, workspace), static_cast<cudaStream_t>(stream));
+}
+
+int nnue_ft_backward_apply(const float* grad0, const float* grad1, int64_t batch, int32_t max_active, int32_t n_persp,
+                           int64_t num_inputs, int32_t output_size, float* weight_grad, float* bias_grad,
+                           int32_t accumulate, void* workspace, size_t workspace_bytes, void* stream) {
+  BwdPlan pl;
+  int rc = make_plan(batch, max_active, num_inputs, output_size, n_persp, pl);
+  if (rc != NNUE_OK) return rc;
+  if (!weight_grad || !bias_grad || (batch > 0 && (!grad0 || (n_persp == 2 && !grad1))))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "backward_apply: null pointer");
+  if (!workspace || workspace_bytes < pl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(NNUE_ERR_WORKSPACE, "backward_apply: workspace missing, misaligned or smaller than %zu bytes",
+                pl.total);
+  return apply_impl(grad0, grad1, pl, carve(pl, workspace), weight_grad, bias_grad, accumulate,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int nnue_ft_backward(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active, const float* grad0,
+                     const float* grad1, int32_t n_persp, int64_t num_inputs, int32_t output_size, float* weight_grad,
+                     float* bias_grad, int32_t accumulate, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = nnue_ft_backward_prepare(idx0, idx1, batch, max_active, n_persp, num_inputs, output_size, workspace,
+                                    workspace_bytes, stream);
+  if (rc != NNUE_OK) return rc;
+  return nnue_ft_backward_apply(grad0, grad1, batch, max_active, n_persp, num_inputs, output_size, weight_grad,
+                                bias_grad, accumulate, workspace, workspace_bytes, stream);
+}
+
+int nnue_ft_quantized_forward_pair(const int32_t* idx0, const int32_t* idx1, int32_t n_persp, int64_t batch,
+                                   int32_t max_active, const int16_t* weight_q, const int32_t* psqt_q,
+                                   int64_t table_rows, int32_t l1, int32_t n_psqt, const int16_t* bias_q,
+                                   int32_t map_training, int16_t* acc0, int16_t* acc1, int32_t* psqt0, int32_t* psqt1,
+                                   void* stream) {
+  if (n_persp != 1 && n_persp != 2) return fail(NNUE_ERR_INVALID_ARGUMENT, "quantized_forward: n_persp must be 1 or 2");
+  if (batch < 0 || max_active < 0 || table_rows <= 0 || table_rows > INT32_MAX || l1 <= 0 || n_psqt < 0)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "quantized_forward: bad sizes");
+  if (l1 % 8 != 0 || n_psqt % 4 != 0 || n_psqt > 128 || l1 > 8 * 32 * 8)
+    return fail(NNUE_ERR_UNSUPPORTED, "quantized_forward: need l1 %% 8 == 0 (<= 2048) and n_psqt %% 4 == 0 (<= 128)");
+  if (batch == 0) return NNUE_OK;
+  if (!idx0 || !weight_q || !psqt_q || !bias_q || !acc0 || !psqt0 ||
+      (n_persp == 2 && (!idx1 || !acc1 || !psqt1)))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "quantized_forward: null pointer");
+  const void* ptrs[] = {weight_q, psqt_q, bias_q, acc0, psqt0, n_persp == 2 ? acc1 : acc0,
+                        n_persp == 2 ? psqt1 : psqt0};
+  for (const void* q : ptrs)
+    if (!aligned16(q)) return fail(NNUE_ERR_INVALID_ARGUMENT, "quantized_forward: pointers must be 16-byte aligned");
+  QFwdParams p{};
+  p.idx[0] = idx0;
+  p.idx[1] = n_persp == 2 ? idx1 : idx0;
+  p.acc[0] = acc0;
+  p.acc[1] = n_persp == 2 ? acc1 : acc0;
+  p.psqt[0] = psqt0;
+  p.psqt[1] = n_persp == 2 ? psqt1 : psqt0;
+  p.Wq = weight_q;
+  p.Pq = psqt_q;
+  p.bias = bias_q;
+  p.B = batch;
+  p.K = max_active;
+  p.Tq = (int32_t)table_rows;
+  p.n8 = l1 / 8;
+  p.np4 = n_psqt / 4;
+  p.P = n_persp;
+  p.map_training = map_training ? 1 : 0;
+  p.items_per_warp = (int32_t)g_tune.fwd_items_per_warp;
+  if (p.np4 > 32) return fail(NNUE_ERR_UNSUPPORTED, "quantized_forward: n_psqt > 128");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch ((p.n8 + 31) / 32) {
+    case 1: launch_qforward_v<1>(p, s); break;
+    case 2: launch_qforward_v<2>(p, s); break;
+    case 3: launch_qforward_v<3>(p, s); break;
+    case 4: launch_qforward_v<4>(p, s); break;
+    case 5: launch_qforward_v<5>(p, s); break;
+    case 6: launch_qforward_v<6>(p, s); break;
+    default: launch_qforward_v<8>(p, s); break;
+  }
+  return check_launch("quantized_forward");
+}
+
+int nnue_ft_halfka_export_quantize(const float* weight, const float* virtual_weight, int32_t l1, int32_t n_psqt,
+                                   float w_scale, float psqt_scale, int16_t* weight_q, int32_t* psqt_q, void* stream) {
+  if (!weight || !weight_q || (n_psqt > 0 && !psqt_q) || l1 <= 0 || n_psqt < 0)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "halfka_export_quantize: bad arguments");
+  // inverse king buckets (halfka_v2_hm.py:9-25): bucket -> oriented king square
+  static const int kKingBuckets[64] = {
+      -1, -1, -1, -1, 31, 30, 29, 28, -1, -1, -1, -1, 27, 26, 25, 24, -1, -1, -1, -1, 23, 22,
+      21, 20, -1, -1, -1, -1, 19, 18, 17, 16, -1, -1, -1, -1, 15, 14, 13, 12, -1, -1, -1, -1,
+      11, 10, 9,  8,  -1, -1, -1, -1, 7,  6,  5,  4,  -1, -1, -1, -1, 3,  2,  1,  0};
+  KingSquares inv{};
+  for (int sq = 0; sq < 64; ++sq)
+    if (kKingBuckets[sq] >= 0) inv.sq[kKingBuckets[sq]] = sq;
+  count_launch();
+  halfka_export_quantize_kernel<<<22528, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      weight, virtual_weight, l1 + n_psqt, l1, w_scale, psqt_scale, inv, weight_q, psqt_q);
+  return check_launch("halfka_export_quantize");
+}
+
+int nnue_ft_quantize_i16(const float* x, int64_t n, float scale, int16_t* q, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !q))) return fail(NNUE_ERR_INVALID_ARGUMENT, "quantize_i16: bad arguments");
+  if (n == 0) return NNUE_OK;
+  count_launch();
+  quantize_i16_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, scale, q);
+  return check_launch("quantize_i16");
+}
+
+}  // extern "C"

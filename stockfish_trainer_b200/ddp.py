@@ -1,0 +1,81 @@
+"""Data-parallel plumbing for the feature-transformer step (torchrun, one
+process per GPU).
+
+Reference behaviour (src/train/common.py:186-199, 256-263 and
+src/train/distributed.py:47-77): the global batch is split evenly over
+ranks, every rank holds the full table, and DDP averages the dense gradients
+with an allreduce.  Here the FT weight and bias gradients live in ONE flat
+fp32 buffer so the exchange is a single collective (or a few row chunks) that
+NCCL runs over NVLink / NVSwitch, followed by the division by world size that
+DDP applies.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class Runtime:
+    rank: int = 0
+    local_rank: int = 0
+    world_size: int = 1
+
+    @property
+    def is_distributed(self) -> bool:
+        return self.world_size > 1
+
+
+def init_from_env(backend: str = "nccl", timeout_s: float = 120.0) -> Runtime:
+    """torchrun environment -> process group (reference distributed.py:47-77)."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if world <= 1:
+        return Runtime()
+    if backend == "nccl":
+        torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        kwargs = {}
+        if backend == "nccl":
+            kwargs["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(backend=backend, init_method="env://",
+                                timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
+    return Runtime(rank=rank, local_rank=local, world_size=world)
+
+
+def shard(global_batch: int, rank: int, world: int) -> tuple[int, int]:
+    """(first position, count) of this rank's even share (common.py:256-263)."""
+    if global_batch % world != 0:
+        raise ValueError(f"global batch {global_batch} is not divisible by world size {world}")
+    n = global_batch // world
+    return rank * n, n
+
+
+class GradientBuffer:
+    """One flat fp32 buffer holding the FT weight gradient [T, C] and the bias
+    gradient [C], so the data-parallel exchange is one collective."""
+
+    def __init__(self, num_inputs: int, output_size: int, device: torch.device):
+        self.flat = torch.empty(num_inputs * output_size + output_size, dtype=torch.float32, device=device)
+        self.weight = self.flat[: num_inputs * output_size].view(num_inputs, output_size)
+        self.bias = self.flat[num_inputs * output_size:]
+
+    def allreduce_mean(self, world_size: int, group=None, chunks: int = 1) -> None:
+        """Sum over ranks then divide by world size (DDP gradient averaging).
+
+        ``chunks`` > 1 splits the buffer into row ranges, each its own
+        collective, so a caller can start reducing finished rows early."""
+        if world_size <= 1:
+            return
+        if chunks <= 1:
+            dist.all_reduce(self.flat, group=group)
+        else:
+            for part in torch.tensor_split(self.flat, chunks):
+                dist.all_reduce(part, group=group)
+        self.flat.div_(world_size)

@@ -1,0 +1,11 @@
+"""Drop-in for src/model/modules/feature_transformer (reference __init__.py:1-5)."""
+
+from .functions import SparseLinearFunction, SparseLinearPairFunction
+from .kernel import make_sparse_input_linear_backward_kernel, make_sparse_input_linear_forward_kernel
+
+__all__ = [
+    "SparseLinearFunction",
+    "SparseLinearPairFunction",
+    "make_sparse_input_linear_forward_kernel",
+    "make_sparse_input_linear_backward_kernel",
+]

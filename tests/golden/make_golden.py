@@ -1,0 +1,146 @@
+"""Generate the golden fixtures in this directory from the REFERENCE itself.
+
+Run once, in a container that has the reference checkout (it is not present
+on the GPU box, so the tests only read the committed ``.npz`` outputs):
+
+    python tests/golden/make_golden.py /path/to/stockfish-trainer
+
+python-chess is not installed, so a stand-in ``chess`` module exposing the
+public constants the reference uses (PAWN..KING = 1..6, WHITE = True,
+BLACK = False, Piece(piece_type, color)) is registered before the import.
+
+Fixtures and the reference code that produced them:
+  halfka_idx.npz              src/model/modules/features/halfka_v2_hm.py:28-37 (_halfka_idx)
+  sorted_backward_inputs.npz  src/model/modules/feature_transformer/kernel.py:108-138
+  quantize_ft.npz             src/model/quantize.py:76-93 (quantize_feature_transformer)
+  export_weights.npz          src/model/modules/features/halfka_v2_hm.py:100-134 (get_export_weights)
+  composed_sizes.npz          src/model/modules/features/composed.py:24-26, full_threats.py, halfka_v2_hm.py
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _install_chess_stub() -> None:
+    chess = types.ModuleType("chess")
+    chess.PAWN, chess.KNIGHT, chess.BISHOP, chess.ROOK, chess.QUEEN, chess.KING = range(1, 7)
+    chess.WHITE, chess.BLACK = True, False
+
+    class Piece:
+        def __init__(self, piece_type, color):
+            self.piece_type = piece_type
+            self.color = color
+
+    chess.Piece = Piece
+    sys.modules["chess"] = chess
+
+
+def main(ref_root: str) -> None:
+    _install_chess_stub()
+    sys.path.insert(0, ref_root)
+    import chess  # the stub
+    from src.model.modules.features import halfka_v2_hm, full_threats, composed
+    from src.model.modules.feature_transformer import kernel
+    from src.model.quantize import QuantizationConfig, QuantizationManager
+
+    # --- HalfKA index table: [pov(white=0, black=1)][ksq][sq][piece id] -------
+    table = np.zeros((2, 64, 64, 12), dtype=np.int32)
+    for pov in range(2):
+        for ksq in range(64):
+            for sq in range(64):
+                for pid in range(12):
+                    p = chess.Piece(pid // 2 + 1, pid % 2 == 0)
+                    table[pov, ksq, sq, pid] = halfka_v2_hm._halfka_idx(pov == 0, ksq, sq, p)
+    np.savez_compressed(os.path.join(HERE, "halfka_idx.npz"), table=table)
+
+    # --- backward preprocessing --------------------------------------------
+    g = torch.Generator().manual_seed(1234)
+    cases = {}
+
+    def rows_unique(B, K, T, fill, compact=True):
+        idx = torch.full((B, K), -1, dtype=torch.int32)
+        for b in range(B):
+            n = int(torch.randint(0, K + 1, (1,), generator=g))
+            n = max(0, min(n, int(K * fill)))
+            vals = torch.randperm(T, generator=g)[:n].to(torch.int32)
+            if compact:
+                idx[b, :n] = vals
+            else:
+                pos = torch.randperm(K, generator=g)[:n]
+                idx[b, pos] = vals
+        return idx
+
+    cases["compact"] = (rows_unique(96, 12, 40, 1.0), 40)
+    cases["holes"] = (rows_unique(80, 16, 300, 0.8, compact=False), 300)
+    cases["empty"] = (torch.full((7, 5), -1, dtype=torch.int32), 10)
+    hot = rows_unique(200, 6, 1000, 1.0)
+    hot[:, 0] = 3  # one feature touched by every position
+    hot[::3, 1] = 999
+    cases["hot"] = (hot, 1000)
+    out = {}
+    for name, (idx, T) in cases.items():
+        flat_bid = kernel._get_flat_batch_indices(idx.shape[0], idx.shape[1], idx.device)
+        sb, sf, sc, ss = kernel._build_sorted_backward_inputs(idx, flat_bid)
+        out[f"{name}_idx"] = idx.numpy()
+        out[f"{name}_T"] = np.int64(T)
+        out[f"{name}_sorted_bid"] = sb.numpy()
+        out[f"{name}_seg_feat"] = sf.numpy()
+        out[f"{name}_seg_count"] = sc.numpy()
+        out[f"{name}_seg_start"] = ss.numpy()
+    np.savez_compressed(os.path.join(HERE, "sorted_backward_inputs.npz"), names=np.array(list(cases)), **out)
+
+    # --- FT quantisation -----------------------------------------------------
+    qm = QuantizationManager(QuantizationConfig())
+    gq = torch.Generator().manual_seed(77)
+    L1, NP, R = 64, 8, 300
+    bias = torch.randn(L1, generator=gq) * 0.05
+    weight = torch.randn(R, L1, generator=gq) * 0.01
+    psqt = torch.randn(R, NP, generator=gq) * 0.2
+    # exact half-way cases: k / 510 * 255 = k / 2 -> ties to even
+    weight[0, :] = torch.arange(L1, dtype=torch.float32) / 510.0
+    weight[1, :] = -torch.arange(L1, dtype=torch.float32) / 510.0
+    bias[:16] = torch.arange(16, dtype=torch.float32) / 510.0
+    psqt[0, :] = torch.tensor([0.5, 1.5, 2.5, -0.5, -1.5, 3.5, 0.0, 7.5]) / 9600.0
+    qb, qw, qp = qm.quantize_feature_transformer(bias, weight, psqt)
+    np.savez_compressed(
+        os.path.join(HERE, "quantize_ft.npz"),
+        bias=bias.numpy(), weight=weight.numpy(), psqt=psqt.numpy(),
+        q_bias=qb.numpy(), q_weight=qw.numpy(), q_psqt=qp.numpy(),
+        ft_quantized_one=np.float64(qm.ft_quantized_one),
+        psqt_scale=np.float64(qm.nnue2score * qm.weight_scale_out),
+    )
+
+    # --- HalfKA export remap (24576 -> 22528 rows) --------------------------
+    torch.manual_seed(5)
+    feat = halfka_v2_hm.HalfKav2Hm(1)
+    with torch.no_grad():
+        feat.virtual_weight.normal_()
+    export = feat.get_export_weights()
+    np.savez_compressed(
+        os.path.join(HERE, "export_weights.npz"),
+        weight=feat.weight.detach().numpy(), virtual=feat.virtual_weight.detach().numpy(),
+        export=export.numpy(),
+    )
+
+    # --- composed feature-set sizes -----------------------------------------
+    ft = composed.combine_input_features(full_threats.FullThreats, halfka_v2_hm.HalfKav2Hm)(16)
+    np.savez_compressed(
+        os.path.join(HERE, "composed_sizes.npz"),
+        num_inputs=np.int64(ft.NUM_INPUTS), max_active=np.int64(ft.MAX_ACTIVE_FEATURES),
+        num_real=np.int64(ft.NUM_REAL_FEATURES), hash=np.int64(ft.HASH),
+        halfka_inputs=np.int64(halfka_v2_hm.HalfKav2Hm.NUM_INPUTS),
+        threat_inputs=np.int64(full_threats.FullThreats.NUM_INPUTS),
+    )
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,163 @@
+"""Backward (device radix CSR + segment sums + bias column sum) vs the oracle.
+
+dW is bit-exact: each feature's sum runs over positions in ascending order,
+like the reference's stable sort + sequential segment kernel, and the two
+perspectives are added once, like autograd adds the reference's two dense
+gradients.  dB is compared with |a - b| <= 1e-6 + 1e-5 |b| (torch's column
+sum order is not reproducible)."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from stockfish_trainer_b200 import _native
+from stockfish_trainer_b200.feature_transformer import ops
+
+from _inputs import feature_batch, random_indices, random_table
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+
+
+def _grads(B, C, seed):
+    rng = np.random.default_rng(seed)
+    return rng.standard_normal((B, C), dtype=np.float32), rng.standard_normal((B, C), dtype=np.float32)
+
+
+def _bwd_pair(i0, i1, g0, g1, T, dev, accumulate=False, dW0=None, dB0=None):
+    C = g0.shape[1]
+    dW = torch.from_numpy(dW0).to(dev) if dW0 is not None else torch.full((T, C), float("nan"), device=dev)
+    dB = torch.from_numpy(dB0).to(dev) if dB0 is not None else torch.full((C,), float("nan"), device=dev)
+    t = lambda a: None if a is None else torch.from_numpy(a).to(dev)
+    ops.backward_into(t(i0), t(i1), t(g0), t(g1), dW, dB, accumulate=accumulate)
+    return dW.cpu().numpy(), dB.cpu().numpy()
+
+
+@pytest.mark.parametrize("fs,B", [("HalfKAv2_hm^", 1500), ("Full_Threats+HalfKAv2_hm^", 800)])
+def test_backward_pair_matches_reference_module_gradient(cuda, fs, B):
+    white, black, T = feature_batch(B, fs, seed=21)
+    C = 1048
+    g0, g1 = _grads(B, C, 22)
+    dW, dB = _bwd_pair(white, black, g0, g1, T, cuda)
+    rW, rB = oracle.ft_backward_pair(white, black, g0, g1, T)
+    np.testing.assert_array_equal(dW, rW)
+    np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
+
+
+def test_backward_single_perspective_accumulates_like_reference_kernel(cuda):
+    T, C, B, K = 500, 72, 900, 20
+    idx = random_indices(B, K, T, seed=5)
+    g, _ = _grads(B, C, 6)
+    dW0 = random_table(T, C, seed=7, std=1.0)
+    dB0 = random_table(1, C, seed=8, std=1.0)[0]
+    dW, dB = _bwd_pair(idx, None, g, None, T, cuda, accumulate=True, dW0=dW0, dB0=dB0)
+    rW, rB = oracle.ft_backward(idx, g, T, dW0.copy(), dB0.copy())
+    np.testing.assert_array_equal(dW, rW)
+    np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("C", [13, 4, 1, 36, 300])
+def test_backward_shapes(cuda, C):
+    T, B, K = 200, 333, 33
+    i0 = random_indices(B, K, T, seed=C)
+    i1 = random_indices(B, K, T, seed=C + 1)
+    g0, g1 = _grads(B, C, C + 2)
+    dW, dB = _bwd_pair(i0, i1, g0, g1, T, cuda)
+    rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
+    np.testing.assert_array_equal(dW, rW)
+    np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
+
+
+def _with_params(params, fn):
+    old = {k: _native.get_param(k) for k in params}
+    try:
+        for k, v in params.items():
+            _native.set_param(k, v)
+        return fn()
+    finally:
+        for k, v in old.items():
+            _native.set_param(k, v)
+
+
+@pytest.mark.parametrize(
+    "params",
+    [
+        {"heavy_threshold": 4, "heavy_cap": 3},  # some heavy rows overflow to the light path
+        {"heavy_threshold": 1, "heavy_cap": 100000},  # nearly every row heavy
+        {"heavy_threshold": 10**9},  # no heavy rows
+        {"bwd_chunk_vec": 0},
+        {"bwd_chunk_vec": 32},
+        {"sort_tile_raw": 512, "sort_tile": 512},
+        {"colsum_parts": 1},
+    ],
+)
+def test_backward_tuning_and_heavy_rows(cuda, params):
+    B, C = 3000, 264
+    T = 700
+    i0 = random_indices(B, 12, T, seed=31, holes=False)
+    i1 = random_indices(B, 12, T, seed=32)
+    i0[:, 0] = 5  # a feature every position uses: 3000-long serial segment
+    i1[::2, 5] = 699
+    g0, g1 = _grads(B, C, 33)
+    # duplicates inside a row are legal: each (position, slot) entry counts once
+    dW, dB = _with_params(params, lambda: _bwd_pair(i0, i1, g0, g1, T, cuda))
+    rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
+    np.testing.assert_array_equal(dW, rW)
+    np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
+
+
+def test_backward_radix_pass_counts(cuda):
+    # T * P <= 1024 -> one digit pass; >= 2^20 -> three passes
+    for T, C in ((100, 8), (600_000, 4)):
+        B, K = 1200, 9
+        i0 = random_indices(B, K, T, seed=T % 97)
+        i1 = random_indices(B, K, T, seed=T % 89)
+        g0, g1 = _grads(B, C, 3)
+        dW, dB = _bwd_pair(i0, i1, g0, g1, T, cuda)
+        rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
+        np.testing.assert_array_equal(dW, rW)
+        np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
+
+
+def test_backward_is_deterministic(cuda):
+    white, black, T = feature_batch(2000, "Full_Threats+HalfKAv2_hm^", seed=41)
+    g0, g1 = _grads(2000, 1048, 42)
+    a = _bwd_pair(white, black, g0, g1, T, cuda)
+    b = _bwd_pair(white, black, g0, g1, T, cuda)
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
+
+
+def test_backward_all_empty(cuda):
+    T, C, B, K = 64, 20, 10, 4
+    idx = np.full((B, K), -1, np.int32)
+    g0, g1 = _grads(B, C, 1)
+    dW, dB = _bwd_pair(idx, idx, g0, g1, T, cuda)
+    assert np.all(dW == 0)
+    np.testing.assert_allclose(dB, g0.astype(np.float64).sum(0) + g1.astype(np.float64).sum(0), rtol=RTOL, atol=ATOL)
+
+
+def test_backward_bad_index_is_skipped_and_flagged(cuda):
+    T, C, B, K = 90, 16, 120, 8
+    idx = random_indices(B, K, T, seed=9)
+    bad = idx.copy()
+    bad[3, 1] = T + 5
+    bad[7, 2] = -3
+    g0, _ = _grads(B, C, 10)
+    _native.device_errors(clear=True)
+    dW, dB = _bwd_pair(bad, None, g0, None, T, cuda)
+    assert _native.device_errors(clear=True) & _native.DEVERR_BAD_INDEX
+    clean = bad.copy()
+    clean[(clean < -1) | (clean >= T)] = -1
+    rW, rB = oracle.ft_backward(clean, g0, T)
+    np.testing.assert_array_equal(dW, rW)
+
+
+def test_backward_workspace_too_small_raises(cuda):
+    T, C, B, K = 50, 8, 10, 4
+    idx = torch.from_numpy(random_indices(B, K, T, seed=1)).to(cuda)
+    ws = torch.empty(64, dtype=torch.uint8, device=cuda)
+    with pytest.raises(_native.NativeError):
+        ops.backward_prepare(idx, None, T, C, ws)

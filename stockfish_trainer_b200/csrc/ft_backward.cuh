@@ -499,60 +499,84 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
 
 // ----------------------------------------------------------------------------
 // Bias gradient: deterministic column sum over positions, both perspectives.
+// Accumulated in float64 (partials over position ranges, then a fixed-order
+// warp tree), so each perspective's sum is within half an fp32 ulp of the
+// exact value; the two perspectives are then rounded and added in fp32, the
+// way autograd adds the reference's two bias gradients (kernel.py:269).
+// torch's own reduction order cannot be reproduced, so this is the closest
+// any implementation can get to it.
 // ----------------------------------------------------------------------------
 struct ColParams {
   const float* dout[2];
   int64_t B;
   int32_t P;
-  int32_t n_vec;
+  int32_t C;         // floats per row
   int32_t parts;
-  float* partial;  // [P][parts][n_vec] vectors
+  int32_t vec4;      // rows are float4-loadable
+  double* partial;   // [P][parts][C]
 };
 
-template <typename VT>
 __global__ void __launch_bounds__(kBlock) colsum_partial_kernel(const ColParams p) {
-  using Ops = Vec<VT>;
   const int part = blockIdx.x, q = blockIdx.y;
   const int64_t r0 = p.B * part / p.parts, r1 = p.B * (part + 1) / p.parts;
-  const VT* __restrict__ src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]);
-  VT* dst = reinterpret_cast<VT*>(p.partial) + ((int64_t)q * p.parts + part) * p.n_vec;
-  for (int col = threadIdx.x; col < p.n_vec; col += blockDim.x) {
-    VT acc = Ops::zero();
-    int64_t r = r0;
-    for (; r + 8 <= r1; r += 8) {
-      VT t[8];
+  const float* __restrict__ src = q ? p.dout[1] : p.dout[0];
+  double* dst = p.partial + ((int64_t)q * p.parts + part) * p.C;
+  if (p.vec4) {
+    const int n4 = p.C / 4;
+    for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x) {
+      double a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+      int64_t r = r0;
+      for (; r + 4 <= r1; r += 4) {
+        float4 t[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) t[i] = Ops::ldg(src + (r + i) * p.n_vec + col);
+        for (int i = 0; i < 4; ++i) t[i] = __ldg(reinterpret_cast<const float4*>(src + (r + i) * p.C) + c4);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) Ops::add(acc, t[i]);
+        for (int i = 0; i < 4; ++i) {
+          a0 += t[i].x;
+          a1 += t[i].y;
+          a2 += t[i].z;
+          a3 += t[i].w;
+        }
+      }
+      for (; r < r1; ++r) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(src + r * p.C) + c4);
+        a0 += t.x;
+        a1 += t.y;
+        a2 += t.z;
+        a3 += t.w;
+      }
+      dst[4 * c4 + 0] = a0;
+      dst[4 * c4 + 1] = a1;
+      dst[4 * c4 + 2] = a2;
+      dst[4 * c4 + 3] = a3;
     }
-    for (; r < r1; ++r) Ops::add(acc, Ops::ldg(src + r * p.n_vec + col));
-    dst[col] = acc;
+  } else {
+    for (int c = threadIdx.x; c < p.C; c += blockDim.x) {
+      double a = 0;
+      for (int64_t r = r0; r < r1; ++r) a += __ldg(src + r * p.C + c);
+      dst[c] = a;
+    }
   }
 }
 
-template <typename VT>
-__global__ void colsum_final_kernel(const float* __restrict__ partial, int32_t P, int32_t parts, int32_t n_vec,
-                                    float* dB, int32_t accumulate) {
-  using Ops = Vec<VT>;
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= n_vec) return;
-  const VT* src = reinterpret_cast<const VT*>(partial);
-  VT tot = Ops::zero();
+// One warp per column: lanes take parts lane, lane+32, ... in order, then a
+// fixed xor-tree; the result is deterministic.
+__global__ void __launch_bounds__(kBlock) colsum_final_kernel(const double* __restrict__ partial, int32_t P,
+                                                              int32_t parts, int32_t C, float* dB,
+                                                              int32_t accumulate) {
+  const int lane = threadIdx.x & 31;
+  const int64_t c = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (c >= C) return;
+  float tot = 0.f;
   for (int q = 0; q < P; ++q) {
-    VT s = Ops::zero();
-    for (int i = 0; i < parts; ++i) Ops::add(s, src[((int64_t)q * parts + i) * n_vec + col]);
-    if (q == 0) tot = s;
-    else Ops::add(tot, s);
+    double s = 0;
+    for (int i = lane; i < parts; i += 32) s += partial[((int64_t)q * parts + i) * C + c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+    const float sf = (float)s;
+    tot = q == 0 ? sf : tot + sf;
   }
-  VT* d = reinterpret_cast<VT*>(dB) + col;
-  if (accumulate) {
-    VT cur = *d;
-    Ops::add(cur, tot);
-    *d = cur;
-  } else {
-    *d = tot;
-  }
+  if (lane == 0) dB[c] = accumulate ? dB[c] + tot : tot;
 }
 
 }  // namespace nnue

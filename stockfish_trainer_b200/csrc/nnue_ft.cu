@@ -48,6 +48,8 @@ int check_launch(const char* what) {
 struct Tuning {
   int64_t fwd_chunk_vec = 64;      // forward column chunk, in 16-byte vectors
   int64_t fwd_items_per_warp = 4;  // (perspective, position) items per warp
+  int64_t fwd_unroll = 4;          // table rows in flight per warp (4 or 8)
+  int64_t bwd_unroll = 4;          // dOut rows in flight per warp, light rows (4 or 8)
   int64_t bwd_chunk_vec = 64;      // backward column chunk, in 16-byte vectors
   int64_t heavy_threshold = 256;   // rows with more entries are split finer
   int64_t heavy_cap = 512;         // at most this many heavy rows per call
@@ -67,6 +69,8 @@ ParamRef* params() {
   static ParamRef p[] = {
       {"fwd_chunk_vec", &g_tune.fwd_chunk_vec, 0, 1 << 20},
       {"fwd_items_per_warp", &g_tune.fwd_items_per_warp, 1, 1024},
+      {"fwd_unroll", &g_tune.fwd_unroll, 4, 8},
+      {"bwd_unroll", &g_tune.bwd_unroll, 4, 8},
       {"bwd_chunk_vec", &g_tune.bwd_chunk_vec, 0, 1 << 20},
       {"heavy_threshold", &g_tune.heavy_threshold, 1, int64_t(1) << 40},
       {"heavy_cap", &g_tune.heavy_cap, 0, 1 << 24},
@@ -82,19 +86,23 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Column geometry.  `chunk` <= 0 or >= n_vec: one chunk.  Otherwise chunks of
-// `chunk` vectors with the remainder folded into the last one.  Chunks are
-// kept >= 8 vectors so the grid's y extent stays small.
+// Column geometry.  Chunks of `chunk` vectors (clamped to [8, 128]) with the
+// remainder folded into the last one, so no chunk is wider than 255 vectors
+// and a lane never needs more than 8 of them (the widest kernel instance).
+// `chunk` <= 0 asks for one chunk per row when the row has <= 256 vectors.
+constexpr int kMaxLaneVectors = 8;
+
 Geom make_geom(int32_t n_vec, int64_t chunk) {
   Geom g;
   g.n_vec = n_vec;
-  if (chunk <= 0 || chunk >= n_vec) {
+  if ((chunk <= 0 || chunk >= n_vec) && n_vec <= 32 * kMaxLaneVectors) {
     g.chunk_vec = n_vec;
     g.n_chunks = 1;
     g.last_vec = n_vec;
     return g;
   }
-  chunk = std::max<int64_t>(chunk, 8);
+  if (chunk <= 0) chunk = 128;
+  chunk = std::min<int64_t>(std::max<int64_t>(chunk, 8), 128);
   g.chunk_vec = (int32_t)chunk;
   g.n_chunks = (int32_t)std::max<int64_t>(1, n_vec / chunk);
   g.last_vec = n_vec - (g.n_chunks - 1) * g.chunk_vec;
@@ -109,15 +117,21 @@ int lanes_per_row(const Geom& g) {  // vectors per lane needed by the widest chu
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
-template <typename VT, int V>
-void launch_forward_v(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
-  constexpr int U = V <= 4 ? 4 : 2;
+template <typename VT, int V, int U>
+void launch_forward_vu(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
   const int64_t n_items = (int64_t)p.P * p.B;
   const int64_t warps = ceil_div(n_items, p.items_per_warp);
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(warps, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
   ft_forward_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
+}
+
+template <typename VT, int V>
+void launch_forward_v(const FwdParams& p, int chunk0, int n_chunks, cudaStream_t s) {
+  if (V <= 2 && g_tune.fwd_unroll >= 8) launch_forward_vu<VT, V, 8>(p, chunk0, n_chunks, s);
+  else if (V <= 4) launch_forward_vu<VT, V, 4>(p, chunk0, n_chunks, s);
+  else launch_forward_vu<VT, V, 2>(p, chunk0, n_chunks, s);
 }
 
 template <typename VT>
@@ -160,13 +174,10 @@ int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int
   p.T = (int32_t)T;
   p.P = P;
   p.items_per_warp = (int32_t)g_tune.fwd_items_per_warp;
-  if (v4) {
-    p.g = make_geom(C / 4, g_tune.fwd_chunk_vec);
-    launch_forward<float4>(p, s);
-  } else {
-    p.g = make_geom(C, g_tune.fwd_chunk_vec * 4);
-    launch_forward<float>(p, s);
-  }
+  p.g = v4 ? make_geom(C / 4, g_tune.fwd_chunk_vec) : make_geom(C, g_tune.fwd_chunk_vec * 4);
+  if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "forward: column chunk too wide");
+  if (v4) launch_forward<float4>(p, s);
+  else launch_forward<float>(p, s);
   return check_launch("forward");
 }
 
@@ -218,7 +229,7 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
   pl.heavy_cap = std::min<int64_t>(g_tune.heavy_cap, T);
   pl.heavy_threshold = g_tune.heavy_threshold;
   pl.parts = std::max<int64_t>(1, std::min<int64_t>(g_tune.colsum_parts, B));
-  const int64_t n_vec_floats = C;  // partial sums stored as floats either way
+  const int64_t n_vec_floats = C;  // float64 partial column sums
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -235,7 +246,7 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
   pl.off_nheavy = take(sizeof(int32_t));
   pl.off_heavy = take(sizeof(int32_t) * pl.heavy_cap);
   pl.off_kind = take(sizeof(uint8_t) * T);
-  pl.off_partial = take(sizeof(float) * P * pl.parts * n_vec_floats);
+  pl.off_partial = take(sizeof(double) * P * pl.parts * n_vec_floats);
   pl.total = o;
   return NNUE_OK;
 }
@@ -243,7 +254,7 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
 struct Ws {
   int32_t *seg, *hist, *bsum, *ka, *va, *kb, *vb, *nheavy, *heavy;
   uint8_t* kind;
-  float* partial;
+  double* partial;
 };
 
 Ws carve(const BwdPlan& pl, void* base) {
@@ -259,7 +270,7 @@ Ws carve(const BwdPlan& pl, void* base) {
   w.nheavy = reinterpret_cast<int32_t*>(b + pl.off_nheavy);
   w.heavy = reinterpret_cast<int32_t*>(b + pl.off_heavy);
   w.kind = reinterpret_cast<uint8_t*>(b + pl.off_kind);
-  w.partial = reinterpret_cast<float*>(b + pl.off_partial);
+  w.partial = reinterpret_cast<double*>(b + pl.off_partial);
   return w;
 }
 
@@ -337,13 +348,19 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
   return check_launch("backward_prepare");
 }
 
-template <typename VT, int V>
-void launch_segsum_v(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
-  constexpr int U = V <= 4 ? 4 : 2;
+template <typename VT, int V, int U>
+void launch_segsum_vu(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(p.T, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
   ft_segsum_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
+}
+
+template <typename VT, int V>
+void launch_segsum_v(const SegParams& p, int chunk0, int n_chunks, cudaStream_t s) {
+  if (V <= 2 && g_tune.bwd_unroll >= 8) launch_segsum_vu<VT, V, 8>(p, chunk0, n_chunks, s);
+  else if (V <= 4) launch_segsum_vu<VT, V, 4>(p, chunk0, n_chunks, s);
+  else launch_segsum_vu<VT, V, 2>(p, chunk0, n_chunks, s);
 }
 
 template <typename VT>
@@ -411,22 +428,22 @@ int device_aux(DeviceAux** out) {
   return NNUE_OK;
 }
 
-template <typename VT>
-void launch_colsum(const float* g0, const float* g1, const BwdPlan& pl, int32_t n_vec, float* partial, float* dB,
+void launch_colsum(const float* g0, const float* g1, const BwdPlan& pl, bool vec4, double* partial, float* dB,
                    int32_t accumulate, cudaStream_t s) {
   ColParams c{};
   c.dout[0] = g0;
   c.dout[1] = pl.P == 2 ? g1 : g0;
   c.B = pl.B;
   c.P = pl.P;
-  c.n_vec = n_vec;
+  c.C = pl.C;
   c.parts = (int32_t)pl.parts;
+  c.vec4 = vec4 ? 1 : 0;
   c.partial = partial;
   count_launch();
-  colsum_partial_kernel<VT><<<dim3((unsigned)pl.parts, (unsigned)pl.P), kBlock, 0, s>>>(c);
+  colsum_partial_kernel<<<dim3((unsigned)pl.parts, (unsigned)pl.P), kBlock, 0, s>>>(c);
   count_launch();
-  colsum_final_kernel<VT><<<(unsigned)ceil_div(n_vec, kBlock), kBlock, 0, s>>>(partial, pl.P, (int32_t)pl.parts,
-                                                                                n_vec, dB, accumulate);
+  colsum_final_kernel<<<(unsigned)ceil_div(pl.C, kWarpsPerBlock), kBlock, 0, s>>>(partial, pl.P, (int32_t)pl.parts,
+                                                                                 pl.C, dB, accumulate);
 }
 
 int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w, float* dW, float* dB,
@@ -448,6 +465,7 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   p.accumulate = accumulate ? 1 : 0;
   p.heavy_cap = (int32_t)pl.heavy_cap;
   p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec) : make_geom(pl.C, g_tune.bwd_chunk_vec * 4);
+  if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "backward: column chunk too wide");
 
   DeviceAux* aux = nullptr;
   int rc = device_aux(&aux);
@@ -459,8 +477,7 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
       return check_launch("backward_apply: fork");
     rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
     if (rc != NNUE_OK) return rc;
-    if (v4) launch_colsum<float4>(g0, g1, pl, pl.C / 4, w.partial, dB, p.accumulate, aux->side);
-    else launch_colsum<float>(g0, g1, pl, pl.C, w.partial, dB, p.accumulate, aux->side);
+    launch_colsum(g0, g1, pl, v4, w.partial, dB, p.accumulate, aux->side);
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
   }
   if (v4) launch_segsum_light<float4>(p, s);

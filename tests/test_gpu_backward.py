@@ -89,6 +89,8 @@ def _with_params(params, fn):
         {"heavy_threshold": 10**9},  # no heavy rows
         {"bwd_chunk_vec": 0},
         {"bwd_chunk_vec": 32},
+        {"bwd_chunk_vec": 128},
+        {"bwd_chunk_vec": 1000},
         {"sort_tile_raw": 512, "sort_tile": 512},
         {"colsum_parts": 1},
     ],
@@ -106,6 +108,26 @@ def test_backward_tuning_and_heavy_rows(cuda, params):
     rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
     np.testing.assert_array_equal(dW, rW)
     np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
+
+
+def test_backward_misaligned_gradients_use_scalar_path(cuda):
+    T, C, B, K = 400, 2052, 500, 10
+    i0 = random_indices(B, K, T, seed=17)
+    i1 = random_indices(B, K, T, seed=18)
+    i0[:, 0] = 3  # one heavy row
+    g0, g1 = _grads(B, C, 19)
+    buf = torch.zeros(2 * B * C + 1, device=cuda)
+    d0 = buf[1:1 + B * C].view(B, C)  # 4-byte offset: scalar path
+    d1 = buf[1 + B * C:].view(B, C)
+    d0.copy_(torch.from_numpy(g0))
+    d1.copy_(torch.from_numpy(g1))
+    dW = torch.empty(T, C, device=cuda)
+    dB = torch.empty(C, device=cuda)
+    ops.backward_into(torch.from_numpy(i0).to(cuda), torch.from_numpy(i1).to(cuda), d0, d1, dW, dB,
+                      accumulate=False)
+    rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
+    np.testing.assert_array_equal(dW.cpu().numpy(), rW)
+    np.testing.assert_allclose(dB.cpu().numpy(), rB, rtol=RTOL, atol=ATOL)
 
 
 def test_backward_radix_pass_counts(cuda):

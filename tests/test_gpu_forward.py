@@ -53,9 +53,10 @@ def test_forward_shapes_and_holes(cuda, C, K):
     np.testing.assert_array_equal(_fwd(idx, W, bias, cuda), oracle.ft_forward(idx, W, bias))
 
 
-def test_forward_misaligned_pointers_use_scalar_path(cuda):
-    T, C, B, K = 120, 64, 300, 16
-    idx = random_indices(B, K, T, seed=7)
+@pytest.mark.parametrize("C", [64, 1048, 2052])
+def test_forward_misaligned_pointers_use_scalar_path(cuda, C):
+    T, B, K = 120, 300, 16
+    idx = random_indices(B, K, T, seed=7 + C)
     W = random_table(T, C, seed=8, std=1.0)
     bias = random_table(1, C, seed=9, std=1.0)[0]
     buf = torch.zeros(T * C + 1, device=cuda)
@@ -78,7 +79,7 @@ def test_forward_empty_rows_and_batches(cuda):
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("chunk,ipw", [(0, 1), (16, 2), (32, 4), (64, 4), (128, 16), (8, 3)])
+@pytest.mark.parametrize("chunk,ipw", [(0, 1), (16, 2), (32, 4), (64, 4), (128, 16), (8, 3), (100, 5), (300, 2)])
 def test_forward_tuning_variants_bit_exact(cuda, chunk, ipw):
     white, _, T = feature_batch(400, "Full_Threats+HalfKAv2_hm^", seed=12)
     C = 1048

@@ -60,8 +60,9 @@ const char *nnue_ft_last_error(void);
  * hot loop. */
 int nnue_ft_device_errors(uint32_t *flags, int clear);
 
-/* Tuning knobs (names: "fwd_chunk_vec", "fwd_items_per_warp", "bwd_chunk_vec",
- * "heavy_threshold", "heavy_cap", "sort_tile_raw", "sort_tile", "colsum_parts").
+/* Tuning knobs (names: "fwd_chunk_vec", "fwd_items_per_warp", "fwd_unroll",
+ * "bwd_chunk_vec", "bwd_unroll", "heavy_threshold", "heavy_cap",
+ * "sort_tile_rows", "sort_tile", "colsum_parts").
  * Process-wide; change them only while no call is in flight and never between
  * a backward_prepare and its backward_apply. */
 int nnue_ft_set_param(const char *name, int64_t value);
@@ -119,6 +120,15 @@ int nnue_ft_backward_apply(const float *grad0, const float *grad1, int64_t batch
                            int32_t n_persp, int64_t num_inputs, int32_t output_size, float *weight_grad,
                            float *bias_grad, int32_t accumulate, void *workspace, size_t workspace_bytes,
                            void *stream);
+
+/* Forward of both perspectives (nnue_ft_forward_pair) plus, concurrently on
+ * the library's side stream, the index-only backward phase
+ * (nnue_ft_backward_prepare with n_persp = 2) into `workspace`.  The caller's
+ * stream waits for both before its next operation; the backward then needs
+ * only nnue_ft_backward_apply with the same sizes and workspace. */
+int nnue_ft_forward_pair_prepare(const int32_t *idx0, const int32_t *idx1, int64_t batch, int32_t max_active,
+                                 const float *weight, int64_t num_inputs, int32_t output_size, const float *bias,
+                                 float *out0, float *out1, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---- quantised (int16) forward ------------------------------------------
  * The inference forward of a serialised net (the engine's accumulator

@@ -37,6 +37,7 @@ _SIGNATURES = {
     "nnue_ft_get_param": (_I64, [ctypes.c_char_p]),
     "nnue_ft_forward": (_I32, [_P, _I64, _I32, _P, _I64, _I32, _P, _P, _P]),
     "nnue_ft_forward_pair": (_I32, [_P, _P, _I64, _I32, _P, _I64, _I32, _P, _P, _P, _P]),
+    "nnue_ft_forward_pair_prepare": (_I32, [_P, _P, _I64, _I32, _P, _I64, _I32, _P, _P, _P, _P, _SZ, _P]),
     "nnue_ft_backward_workspace_size": (_SZ, [_I64, _I32, _I64, _I32, _I32]),
     "nnue_ft_backward": (_I32, [_P, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I32, _P, _SZ, _P]),
     "nnue_ft_backward_prepare": (_I32, [_P, _P, _I64, _I32, _I32, _I64, _I32, _P, _SZ, _P]),

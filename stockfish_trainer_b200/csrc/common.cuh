@@ -58,20 +58,20 @@ struct Vec<float> {
   static __device__ __forceinline__ void st_stream(float* p, const float& v) { __stcs(p, v); }
 };
 
-// Column chunking of one table row of n_vec vectors.  Chunk c covers vectors
-// [c * chunk_vec, c * chunk_vec + width(c)); the last chunk absorbs the
-// remainder.  Chunks are the OUTER grid dimension, so at any moment the
+// Column chunking of one table row of n_vec vectors into n_chunks balanced
+// chunks: chunk c covers vectors [begin(c), begin(c + 1)), widths differ by
+// at most one.  Chunks are the OUTER grid dimension, so at any moment the
 // running blocks touch one column slice of the table / gradient -- a slice
 // sized to stay resident in L2 while it is re-read.
 struct Geom {
   int32_t n_vec;
-  int32_t chunk_vec;
   int32_t n_chunks;
-  int32_t last_vec;
-  __host__ __device__ __forceinline__ int begin(int c) const { return c * chunk_vec; }
-  __host__ __device__ __forceinline__ int width(int c) const {
-    return c == n_chunks - 1 ? last_vec : chunk_vec;
+  int32_t max_width;  // widest chunk, in vectors
+  int32_t exact;      // 1: chunks of exactly max_width vectors + a narrower tail; 0: balanced widths
+  __host__ __device__ __forceinline__ int begin(int c) const {
+    return exact ? (c < n_chunks ? c * max_width : n_vec) : (int)(((int64_t)c * n_vec) / n_chunks);
   }
+  __host__ __device__ __forceinline__ int width(int c) const { return begin(c + 1) - begin(c); }
 };
 
 // Warp / block reductions and scans on int32.

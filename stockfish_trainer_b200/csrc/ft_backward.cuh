@@ -139,8 +139,7 @@ struct PassParams {
   const int32_t* in_keys;    // later passes
   const int32_t* in_vals;
   const int32_t* count;      // later passes: device count of valid entries
-  int64_t n_src;             // first pass: P * B * K
-  int32_t tile;              // entries per warp tile, multiple of 32 * kSortBatch
+  int32_t tile;              // first pass: index rows per warp; later: entries per warp (multiple of 32*kSortBatch)
   int32_t shift;             // digit = (key >> shift) & (bins - 1)
   int32_t bits;
   int32_t* tile_hist;        // [bins][n_tiles]
@@ -150,60 +149,76 @@ struct PassParams {
   int64_t out_cap;           // capacity of out_keys / out_vals
 };
 
-constexpr int kSortBatch = 16;  // rounds of 32 entries loaded before they are processed
+constexpr int kSortBatch = 16;  // 32-slot chunks loaded before they are processed
 
-__device__ __forceinline__ void raw_entry(const RawSrc& s, int64_t e, int& key, int& b, bool& valid) {
-  const int persp = e >= s.n_raw ? 1 : 0;
-  const int r = (int)(e - (int64_t)persp * s.n_raw);
-  const int f = __ldcs((persp ? s.idx[1] : s.idx[0]) + r);
-  valid = (unsigned)f < (unsigned)s.T;
-  if (!valid && f != -1) flag_error(kErrBadIndex);
-  key = f * s.P + persp;
-  b = r / s.K;
+// ---- first pass: walk the raw [P][B][K] index arrays row by row ------------
+// A warp tile is `tile` consecutive index rows (perspective-major, then
+// position).  Each row is read in chunks of 32 slots, kSortBatch chunks per
+// batch of loads; a chunk with no valid slot (the -1 tail) costs one ballot.
+// Entries are visited in (perspective, position, slot) order, so ranks are
+// stable.
+struct RowWalk {
+  int64_t row;  // global row = perspective * B + position
+  int kc;       // 32-slot chunk inside the row
+};
+
+__device__ __forceinline__ void raw_load_batch(const PassParams& p, RowWalk w, int64_t r_end, int KC, int lane,
+                                               int (&f)[kSortBatch], int (&persp)[kSortBatch],
+                                               int (&b)[kSortBatch]) {
+  const int64_t B = p.raw.n_raw / (p.raw.K > 0 ? p.raw.K : 1);
+#pragma unroll
+  for (int r = 0; r < kSortBatch; ++r) {
+    f[r] = -1;
+    persp[r] = 0;
+    b[r] = 0;
+    if (w.row < r_end) {
+      const int q = w.row >= B ? 1 : 0;
+      const int64_t pos = w.row - q * B;
+      const int k = w.kc * 32 + lane;
+      persp[r] = q;
+      b[r] = (int)pos;
+      if (k < p.raw.K) f[r] = __ldcs((q ? p.raw.idx[1] : p.raw.idx[0]) + pos * p.raw.K + k);
+      if (++w.kc == KC) {
+        w.kc = 0;
+        ++w.row;
+      }
+    }
+  }
 }
 
-template <bool RAW>
-__device__ __forceinline__ int64_t pass_n_src(const PassParams& p) {
-  return RAW ? p.n_src : (int64_t)*p.count;
+__device__ __forceinline__ RowWalk advance(RowWalk w, int KC, int n) {
+  const int64_t t = (int64_t)w.kc + n;
+  w.row += t / KC;
+  w.kc = (int)(t % KC);
+  return w;
 }
 
-template <bool RAW>
-__global__ void __launch_bounds__(kBlock) sort_hist_kernel(const PassParams p) {
+__global__ void __launch_bounds__(kBlock) sort_hist_rows_kernel(const PassParams p) {
   extern __shared__ int32_t sh[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bins = 1 << p.bits;
   int32_t* h = sh + warp * bins;
   for (int i = lane; i < bins; i += 32) h[i] = 0;
   __syncwarp();
-  const int64_t n_src = pass_n_src<RAW>(p);
-  const int64_t n_tiles = (n_src + p.tile - 1) / p.tile;
+  const int64_t rows = (int64_t)p.raw.P * (p.raw.n_raw / (p.raw.K > 0 ? p.raw.K : 1));
+  const int64_t n_tiles = (rows + p.tile - 1) / p.tile;
   const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (tile >= n_tiles) return;  // whole warp
-  const int64_t e0 = tile * p.tile;
-  const int64_t e1 = e0 + p.tile < n_src ? e0 + p.tile : n_src;
-  for (int64_t base = e0; base < e1; base += 32 * kSortBatch) {
-    int key[kSortBatch];
-    bool valid[kSortBatch];
+  if (tile >= n_tiles) return;
+  const int KC = (p.raw.K + 31) / 32;
+  const int64_t r0 = tile * p.tile;
+  const int64_t r1 = r0 + p.tile < rows ? r0 + p.tile : rows;
+  for (RowWalk w{r0, 0}; w.row < r1; w = advance(w, KC, kSortBatch)) {
+    int f[kSortBatch], persp[kSortBatch], b[kSortBatch];
+    raw_load_batch(p, w, r1, KC, lane, f, persp, b);
 #pragma unroll
     for (int r = 0; r < kSortBatch; ++r) {
-      const int64_t e = base + r * 32 + lane;
-      valid[r] = false;
-      key[r] = 0;
-      if (e < e1) {
-        if (RAW) {
-          int b;
-          raw_entry(p.raw, e, key[r], b, valid[r]);
-        } else {
-          key[r] = __ldg(p.in_keys + e);
-          valid[r] = true;
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < kSortBatch; ++r) {
-      if (valid[r]) {
-        atomicAdd(&h[(key[r] >> p.shift) & (bins - 1)], 1);
-        if (RAW && p.key_count) atomicAdd(&p.key_count[key[r]], 1);
+      const bool valid = (unsigned)f[r] < (unsigned)p.raw.T;
+      if (!valid && f[r] != -1) flag_error(kErrBadIndex);
+      if (__ballot_sync(kFull, valid) == 0) continue;
+      if (valid) {
+        const int key = f[r] * p.raw.P + persp[r];
+        atomicAdd(&h[(key >> p.shift) & (bins - 1)], 1);
+        if (p.key_count) atomicAdd(&p.key_count[key], 1);
       }
     }
   }
@@ -211,17 +226,94 @@ __global__ void __launch_bounds__(kBlock) sort_hist_kernel(const PassParams p) {
   for (int i = lane; i < bins; i += 32) p.tile_hist[(int64_t)i * n_tiles + tile] = h[i];
 }
 
-template <bool RAW>
+// Appends one 32-wide round of (key, value) pairs to the per-digit runs.
+__device__ __forceinline__ void scatter_round(const PassParams& p, int32_t* h, int bins, bool valid, int key, int val,
+                                              unsigned lt) {
+  const int digit = valid ? ((key >> p.shift) & (bins - 1)) : bins;  // `bins` = no digit
+  const unsigned peers = __match_any_sync(kFull, digit);
+  const int rank = __popc(peers & lt);
+  const int dst0 = valid ? h[digit] : 0;
+  __syncwarp();
+  if (valid) {
+    const int dst = dst0 + rank;
+    if ((unsigned long long)(unsigned)dst < (unsigned long long)p.out_cap) {
+      if (p.out_keys) p.out_keys[dst] = key;
+      p.out_vals[dst] = val;
+    } else {
+      flag_error(kErrBadSegment);
+    }
+    if (rank == 0) h[digit] = dst0 + __popc(peers);
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kBlock) sort_scatter_rows_kernel(const PassParams p) {
+  extern __shared__ int32_t sh[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bins = 1 << p.bits;
+  int32_t* h = sh + warp * bins;  // running destination per digit
+  const int64_t rows = (int64_t)p.raw.P * (p.raw.n_raw / (p.raw.K > 0 ? p.raw.K : 1));
+  const int64_t n_tiles = (rows + p.tile - 1) / p.tile;
+  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (tile >= n_tiles) return;
+  // tile_hist now holds the scanned offsets: start of (digit, tile).
+  for (int i = lane; i < bins; i += 32) h[i] = p.tile_hist[(int64_t)i * n_tiles + tile];
+  __syncwarp();
+  const int KC = (p.raw.K + 31) / 32;
+  const int64_t r0 = tile * p.tile;
+  const int64_t r1 = r0 + p.tile < rows ? r0 + p.tile : rows;
+  const unsigned lt = lanemask_lt();
+  for (RowWalk w{r0, 0}; w.row < r1; w = advance(w, KC, kSortBatch)) {
+    int f[kSortBatch], persp[kSortBatch], b[kSortBatch];
+    raw_load_batch(p, w, r1, KC, lane, f, persp, b);
+#pragma unroll
+    for (int r = 0; r < kSortBatch; ++r) {
+      const bool valid = (unsigned)f[r] < (unsigned)p.raw.T;
+      if (__ballot_sync(kFull, valid) == 0) continue;
+      const int64_t B = p.raw.n_raw / p.raw.K;
+      scatter_round(p, h, bins, valid, f[r] * p.raw.P + persp[r], (int)(persp[r] * B + b[r]), lt);
+    }
+  }
+}
+
+// ---- later passes: flat (key, value) arrays of device-known length ---------
+__global__ void __launch_bounds__(kBlock) sort_hist_kernel(const PassParams p) {
+  extern __shared__ int32_t sh[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bins = 1 << p.bits;
+  int32_t* h = sh + warp * bins;
+  for (int i = lane; i < bins; i += 32) h[i] = 0;
+  __syncwarp();
+  const int64_t n_src = *p.count;
+  const int64_t n_tiles = (n_src + p.tile - 1) / p.tile;
+  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (tile >= n_tiles) return;  // whole warp
+  const int64_t e0 = tile * p.tile;
+  const int64_t e1 = e0 + p.tile < n_src ? e0 + p.tile : n_src;
+  for (int64_t base = e0; base < e1; base += 32 * kSortBatch) {
+    int key[kSortBatch];
+#pragma unroll
+    for (int r = 0; r < kSortBatch; ++r) {
+      const int64_t e = base + r * 32 + lane;
+      key[r] = e < e1 ? __ldg(p.in_keys + e) : -1;
+    }
+#pragma unroll
+    for (int r = 0; r < kSortBatch; ++r)
+      if (key[r] >= 0) atomicAdd(&h[(key[r] >> p.shift) & (bins - 1)], 1);
+  }
+  __syncwarp();
+  for (int i = lane; i < bins; i += 32) p.tile_hist[(int64_t)i * n_tiles + tile] = h[i];
+}
+
 __global__ void __launch_bounds__(kBlock) sort_scatter_kernel(const PassParams p) {
   extern __shared__ int32_t sh[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bins = 1 << p.bits;
   int32_t* h = sh + warp * bins;  // running destination per digit
-  const int64_t n_src = pass_n_src<RAW>(p);
+  const int64_t n_src = *p.count;
   const int64_t n_tiles = (n_src + p.tile - 1) / p.tile;
   const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
   if (tile >= n_tiles) return;
-  // tile_hist now holds the scanned offsets: start of (digit, tile).
   for (int i = lane; i < bins; i += 32) h[i] = p.tile_hist[(int64_t)i * n_tiles + tile];
   __syncwarp();
   const int64_t e0 = tile * p.tile;
@@ -229,46 +321,26 @@ __global__ void __launch_bounds__(kBlock) sort_scatter_kernel(const PassParams p
   const unsigned lt = lanemask_lt();
   for (int64_t base = e0; base < e1; base += 32 * kSortBatch) {
     int key[kSortBatch], val[kSortBatch];
-    bool valid[kSortBatch];
 #pragma unroll
     for (int r = 0; r < kSortBatch; ++r) {
       const int64_t e = base + r * 32 + lane;
-      valid[r] = false;
-      key[r] = 0;
+      key[r] = -1;
       val[r] = 0;
       if (e < e1) {
-        if (RAW) {
-          raw_entry(p.raw, e, key[r], val[r], valid[r]);
-        } else {
-          key[r] = __ldg(p.in_keys + e);
-          val[r] = __ldg(p.in_vals + e);
-          valid[r] = true;
-        }
+        key[r] = __ldg(p.in_keys + e);
+        val[r] = __ldg(p.in_vals + e);
       }
     }
 #pragma unroll
     for (int r = 0; r < kSortBatch; ++r) {
-      const int digit = valid[r] ? ((key[r] >> p.shift) & (bins - 1)) : bins;  // `bins` = no digit
-      const unsigned peers = __match_any_sync(kFull, digit);
-      const int rank = __popc(peers & lt);
-      const int dst0 = valid[r] ? h[digit] : 0;
-      __syncwarp();
-      if (valid[r]) {
-        const int dst = dst0 + rank;
-        if ((unsigned long long)(unsigned)dst < (unsigned long long)p.out_cap) {
-          if (p.out_keys) p.out_keys[dst] = key[r];
-          p.out_vals[dst] = val[r];
-        } else {
-          flag_error(kErrBadSegment);
-        }
-        if (rank == 0) h[digit] = dst0 + __popc(peers);
-      }
-      __syncwarp();
+      if (base + r * 32 >= e1) break;  // uniform
+      scatter_round(p, h, bins, key[r] >= 0, key[r], val[r], lt);
     }
   }
 }
 
-// Rows with more than `threshold` entries (both perspectives) are heavy.
+// Rows with more than `threshold` entries (both perspectives) are heavy
+// (used by the fallback walk path only).
 __global__ void classify_rows_kernel(const int32_t* __restrict__ seg_start, int32_t T, int32_t P,
                                      int32_t threshold, int32_t cap, int32_t* __restrict__ n_heavy,
                                      int32_t* __restrict__ heavy_list, uint8_t* __restrict__ row_kind) {
@@ -286,41 +358,64 @@ __global__ void classify_rows_kernel(const int32_t* __restrict__ seg_start, int3
   row_kind[f] = kind;
 }
 
+// Streaming work split: warp w owns the rows whose first entry lies in
+// [w * epw, (w + 1) * epw), i.e. rows [first_row[w], first_row[w + 1]).
+// Row f is the first row of every w with seg(f - 1) < w * epw <= seg(f), so
+// each first_row entry has exactly one writer.  n_warps is the grid's
+// capacity; warps past the last entry get empty ranges (first_row = T).
+__global__ void warp_ranges_kernel(const int32_t* __restrict__ seg_start, int32_t T, int32_t P, int32_t epw,
+                                   int32_t n_warps, int32_t* __restrict__ first_row) {
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f > T) return;
+  const int64_t prev = f == 0 ? -1 : seg_start[(f - 1) * P];
+  const int64_t lo = f == 0 ? 0 : prev / epw + 1;
+  const int64_t hi = f == T ? n_warps : seg_start[f * P] / epw;
+  for (int64_t w = lo; w <= hi && w <= n_warps; ++w) first_row[w] = (int32_t)f;
+}
+
 // ----------------------------------------------------------------------------
-// Segment sums
+// Segment sums.  Sorted values encode (perspective, position) as
+// perspective * B + b, so a load can be issued from the value alone.
 // ----------------------------------------------------------------------------
 struct SegParams {
   const float* dout[2];       // [B, C] per perspective
-  const int32_t* sorted_b;    // positions, grouped by key, ascending b within a key
+  const int32_t* sorted_b;    // perspective * B + position, grouped by key, ascending within a key
   const int32_t* seg_start;   // [T * P + 1]
-  const int32_t* heavy_list;
+  const int32_t* heavy_list;  // walk path only
   const int32_t* n_heavy;
   const uint8_t* row_kind;
+  const int32_t* first_row;   // stream path: [n_stream_warps + 1]
   float* dW;                  // [T, C]
-  int64_t B;                  // positions: every sorted value must lie in [0, B)
+  int64_t B;                  // positions per perspective
   int32_t T;
   int32_t P;
   int32_t accumulate;         // 0: dW[f] = sum (all rows written); 1: dW[f] += sum (touched rows)
   int32_t heavy_cap;
   int32_t chunk0;             // first column chunk of this launch (blockIdx.y offset)
+  int32_t n_stream_warps;
   Geom g;
 };
 
-// acc[v] += dOut[b, cols] for every b in sorted_b[s, e), ascending.
-// Sorted values outside [0, B) would mean a corrupted workspace; they are
-// skipped and flagged rather than dereferenced.
+// Decodes a sorted value of perspective q; out-of-range values (a corrupt
+// workspace) are flagged and returned as -1, never dereferenced.
+__device__ __forceinline__ int decode_position(int v, int q, int64_t B) {
+  const int64_t b = (int64_t)v - (int64_t)q * B;
+  if ((unsigned long long)b >= (unsigned long long)B) {
+    flag_error(kErrBadSegment);
+    return -1;
+  }
+  return (int)b;
+}
+
+// acc[v] += dOut_q[b, cols] for every entry of sorted_b[s, e) (perspective q), ascending.
 template <typename VT, int V, int U>
 __device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src, int64_t row_vec,
-                                        const int32_t* __restrict__ sb, int s, int e, int64_t B,
+                                        const int32_t* __restrict__ sb, int s, int e, int q, int64_t B,
                                         const bool (&ok)[V], int lane) {
   using Ops = Vec<VT>;
   for (int j0 = s; j0 < e; j0 += 32) {
     const int cnt = e - j0 < 32 ? e - j0 : 32;
-    int my = lane < cnt ? __ldg(sb + j0 + lane) : 0;
-    if ((unsigned long long)(unsigned)my >= (unsigned long long)B) {
-      flag_error(kErrBadSegment);
-      my = -1;
-    }
+    const int my = lane < cnt ? decode_position(__ldg(sb + j0 + lane), q, B) : -1;
     for (int u0 = 0; u0 < cnt; u0 += U) {
       int rows[U];
       bool has[U];
@@ -346,11 +441,10 @@ __device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src
 
 template <typename VT, int V>
 __device__ __forceinline__ void seg_write(const SegParams& p, int64_t f, int col, const VT (&tot)[V],
-                                          const bool (&ok)[V]) {
+                                          const bool (&ok)[V], bool touched) {
   using Ops = Vec<VT>;
   VT* dst = reinterpret_cast<VT*>(p.dW) + f * (int64_t)p.g.n_vec + col;
   if (p.accumulate) {
-    const bool touched = p.seg_start[(f + 1) * p.P] > p.seg_start[f * p.P];
     if (!touched) return;
 #pragma unroll
     for (int v = 0; v < V; ++v)
@@ -366,10 +460,12 @@ __device__ __forceinline__ void seg_write(const SegParams& p, int64_t f, int col
   }
 }
 
-// Light rows: one warp per (row, column chunk), V vectors per lane, U rows of
-// dOut in flight.  Heavy rows are skipped here (ft_segsum_heavy_kernel).
+// Fallback light rows (any geometry / the scalar path): one warp per (row,
+// column chunk); per perspective the row's entries are read 32 at a time and
+// broadcast with __shfl_sync, U dOut rows in flight per batch.  Heavy rows
+// are left to ft_segsum_heavy_kernel.
 template <typename VT, int V, int U>
-__global__ void __launch_bounds__(kBlock) ft_segsum_kernel(const SegParams p) {
+__global__ void __launch_bounds__(kBlock) ft_segsum_walk_kernel(const SegParams p) {
   using Ops = Vec<VT>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunk = p.chunk0 + blockIdx.y;
@@ -391,29 +487,22 @@ __global__ void __launch_bounds__(kBlock) ft_segsum_kernel(const SegParams p) {
     for (int v = 0; v < V; ++v) acc[v] = Ops::zero();
     const int s = p.seg_start[f * p.P + q], e = p.seg_start[f * p.P + q + 1];
     const VT* src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]) + c0 + lane;
-    seg_sum<VT, V, U>(acc, src, row_vec, p.sorted_b, s, e, p.B, ok, lane);
+    seg_sum<VT, V, U>(acc, src, row_vec, p.sorted_b, s, e, q, p.B, ok, lane);
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       if (q == 0) tot[v] = acc[v];
       else Ops::add(tot[v], acc[v]);
     }
   }
-  seg_write<VT, V>(p, f, c0 + lane, tot, ok);
+  const bool touched = p.seg_start[(f + 1) * p.P] > p.seg_start[f * p.P];
+  seg_write<VT, V>(p, f, c0 + lane, tot, ok, touched);
 }
 
 // ---------------------------------------------------------------------------
-// Heavy rows.  A row that thousands of positions share is a long serial sum
-// per column (the reference order is ascending b, which the result must keep),
-// so the only parallelism is across columns.  Each warp owns one 32-vector
-// piece of a column chunk and streams the dOut rows through a private
-// shared-memory ring with cp.async: every lane copies its own 16 bytes of
-// entry j into slot j % kHeavyStages and later reads back only what it
-// copied, so no barrier is needed and kHeavyStages entries stay in flight
-// per warp without holding registers.
+// cp.async helpers: every lane copies its own 16 (or 4) bytes into a lane-
+// private shared-memory slot and later reads back only what it copied, so
+// no barrier is needed; the group count bounds what is still in flight.
 // ---------------------------------------------------------------------------
-constexpr int kHeavyWarps = 2;
-constexpr int kHeavyStages = 48;
-
 template <typename VT>
 __device__ __forceinline__ void cp_async_vec(VT* smem_dst, const VT* gsrc, bool pred);
 
@@ -437,6 +526,11 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
+
+// Heavy rows of the fallback path: one warp per 32-vector piece of a column
+// chunk streams the row's dOut slices through a kHeavyStages-deep ring.
+constexpr int kHeavyWarps = 2;
+constexpr int kHeavyStages = 48;
 
 template <typename VT>
 __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const SegParams p) {
@@ -462,20 +556,17 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
     const int s = p.seg_start[f * p.P + q], e = p.seg_start[f * p.P + q + 1];
     const VT* src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]) + (ok1 ? col : 0);
     VT acc = Ops::zero();
-    // issue pointer t runs kHeavyStages entries ahead of the consume pointer j
-    int t = s;
-    int idx_base = -1, my_b = 0;
+    int t = s;  // issue pointer, kHeavyStages entries ahead of the consume pointer
+    int idx_base = -1, my_b = -1;
     auto issue = [&](int slot_i) {
       if (t < e) {
         const int base = t & ~31;
         if (base != idx_base) {
           idx_base = base;
-          my_b = base + lane < e ? __ldg(p.sorted_b + base + lane) : 0;
+          my_b = base + lane < e && base + lane >= s ? decode_position(__ldg(p.sorted_b + base + lane), q, p.B) : -1;
         }
         const int b = __shfl_sync(kFull, my_b, t & 31);
-        const bool in_range = (unsigned long long)(unsigned)b < (unsigned long long)p.B;
-        if (!in_range) flag_error(kErrBadSegment);
-        cp_async_vec<VT>(ring + slot_i * 32, src + (in_range ? (int64_t)b * row_vec : 0), ok1 && in_range);
+        cp_async_vec<VT>(ring + slot_i * 32, src + (b >= 0 ? (int64_t)b * row_vec : 0), ok1 && b >= 0);
       }
       cp_async_commit();  // empty groups keep the pending count constant
       ++t;
@@ -494,7 +585,149 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
   }
   const bool ok[1] = {ok1};
   const VT t1[1] = {tot};
-  seg_write<VT, 1>(p, f, col, t1, ok);
+  seg_write<VT, 1>(p, f, col, t1, ok, true);
+}
+
+// ---------------------------------------------------------------------------
+// Streaming segment sums (fast path: 16-byte vectors, chunks of <= 32 x SV
+// vectors).  Each warp owns a contiguous range of rows holding about
+// `entries per warp` entries; because rows are in key order, their entries
+// are one contiguous run of the sorted list.  The warp streams that run
+// through a lane-private cp.async ring kStreamStages entries deep (SV
+// vectors per lane per entry), adding each arriving dOut slice to the
+// current (row, perspective) accumulator and finishing a row when its last
+// segment ends -- the pipeline never drains between rows, and hot rows need
+// no special path.  Values decode to (perspective, position) at issue time;
+// the consume side walks the segment table, 32 boundaries per load.
+// ---------------------------------------------------------------------------
+// 16-byte cp.async, skipped entirely when !pred (the destination keeps its
+// old bytes; callers never use them).
+__device__ __forceinline__ void cp_async16_if(float4* smem_dst, const float4* gsrc, bool pred) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p cp.async.cg.shared.global [%0], [%1], 16;\n}\n" ::"r"(d),
+      "l"(gsrc), "r"((int)pred)
+      : "memory");
+}
+
+// S: ring stages per warp, G: entries per commit group, WPB: warps per block.
+template <int SV, int S, int G, int WPB>
+__global__ void __launch_bounds__(32 * WPB) ft_segsum_stream_kernel(const SegParams p) {
+  using Ops = Vec<float4>;
+  static_assert(S % G == 0, "stages must be a multiple of the group size");
+  extern __shared__ __align__(16) unsigned char stream_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4* ring = reinterpret_cast<float4*>(stream_smem) + (warp * S * SV) * 32 + lane;
+  const int chunk = p.chunk0 + blockIdx.y;
+  const int c0 = p.g.begin(chunk);
+  const int width = p.g.width(chunk);
+  bool ok[SV];
+#pragma unroll
+  for (int v = 0; v < SV; ++v) ok[v] = lane + 32 * v < width;
+  const int w = blockIdx.x * WPB + warp;
+  if (w >= p.n_stream_warps) return;
+  const int f_begin = p.first_row[w], f_end = p.first_row[w + 1];
+  if (f_begin >= f_end) return;
+  const int64_t row_vec = p.g.n_vec;
+  const int P = p.P;
+  const int Bi = (int)p.B;
+  const float4* __restrict__ d0 = reinterpret_cast<const float4*>(p.dout[0]) + c0 + lane;
+  const float4* __restrict__ d1 = reinterpret_cast<const float4*>(P == 2 ? p.dout[1] : p.dout[0]) + c0 + lane;
+  const int E0 = p.seg_start[(int64_t)f_begin * P];
+  const int E1 = p.seg_start[(int64_t)f_end * P];
+
+  // ---- issue side: entry t -> ring slot (t - E0) % S, G entries per group
+  int t = E0, idx_base = -1, my_v = 0;
+  auto issue = [&](int slot_i) {
+    if (t < E1) {
+      const int base = t & ~31;
+      if (base != idx_base) {
+        idx_base = base;
+        my_v = base + lane < E1 ? __ldg(p.sorted_b + base + lane) : 0;
+      }
+      const int v = __shfl_sync(kFull, my_v, t & 31);
+      const int q = v >= Bi ? 1 : 0;
+      const int b = v - q * Bi;
+      const bool good = (unsigned)b < (unsigned)Bi;
+      if (!good) flag_error(kErrBadSegment);
+      const float4* src = (q ? d1 : d0) + (good ? (int64_t)b * row_vec : 0);
+#pragma unroll
+      for (int s = 0; s < SV; ++s) cp_async16_if(ring + (slot_i * SV + s) * 32, src + 32 * s, ok[s] && good);
+    }
+    ++t;
+  };
+#pragma unroll 1
+  for (int i = 0; i < S; i += G) {
+#pragma unroll
+    for (int e = 0; e < G; ++e) issue(i + e);
+    cp_async_commit();
+  }
+
+  // ---- consume side: segment boundaries of keys [f_begin * P, f_end * P]
+  int key = f_begin * P;
+  int bnd_base = -1, my_bnd = 0;
+  auto seg_end = [&](int k) {  // end of segment k = seg_start[k + 1]
+    const int idx = k + 1;
+    const int base = idx & ~31;
+    if (base != bnd_base) {
+      bnd_base = base;
+      my_bnd = p.seg_start[base + lane < p.T * P + 1 ? base + lane : p.T * P];
+    }
+    return __shfl_sync(kFull, my_bnd, idx & 31);
+  };
+  float4 acc[SV], tot[SV];
+#pragma unroll
+  for (int s = 0; s < SV; ++s) acc[s] = tot[s] = Ops::zero();
+  int end = seg_end(key);
+  int row_first = E0;
+  int j = E0, stage = 0;
+  bool done = false;
+  while (!done) {
+    cp_async_wait<S / G - 1>();  // the oldest group (G entries) has landed
+#pragma unroll
+    for (int e = 0; e < G; ++e) {
+      // close every segment that ends at j (empty segments and rows included)
+      while (!done && end == j) {
+        const int q = key - (key / P) * P;
+        if (q == 0) {
+#pragma unroll
+          for (int s = 0; s < SV; ++s) tot[s] = acc[s];
+        } else {
+#pragma unroll
+          for (int s = 0; s < SV; ++s) Ops::add(tot[s], acc[s]);
+        }
+#pragma unroll
+        for (int s = 0; s < SV; ++s) acc[s] = Ops::zero();
+        if (q == P - 1) {
+          const int64_t f = key / P;
+          seg_write<float4, SV>(p, f, c0 + lane, tot, ok, j > row_first);
+          row_first = j;
+          if (f + 1 >= f_end) done = true;
+        }
+        if (!done) {
+          ++key;
+          end = seg_end(key);
+        }
+      }
+      // a segment table that is not monotone (corrupt workspace) ends the walk
+      if (!done && (end < j || (j >= E1 && end != j))) {
+        flag_error(kErrBadSegment);
+        done = true;
+      }
+      if (!done && j < E1) {
+#pragma unroll
+        for (int s = 0; s < SV; ++s) Ops::add(acc[s], ring[((stage + e) * SV + s) * 32]);
+        ++j;
+      }
+    }
+    if (done) break;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < G; ++e) issue(stage + e);
+    cp_async_commit();
+    stage = stage + G == S ? 0 : stage + G;
+  }
+  cp_async_wait<0>();
 }
 
 // ----------------------------------------------------------------------------

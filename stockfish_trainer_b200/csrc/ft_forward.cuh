@@ -5,11 +5,14 @@
 // in fp32, one add per active feature in ascending k -- the same order as the
 // reference, so the result is bit-identical.
 //
-// Mapping: one warp per (perspective, position) item and column chunk.  The
-// warp reads 32 indices with one coalesced load, ballots the valid ones and
-// walks them in ascending k, U rows at a time: all U x V 128-bit row loads
-// are issued before the U x V adds, so each lane keeps U*V loads in flight.
-// Lanes own fixed column vectors, which keeps the per-column add order.
+// Mapping: one warp per (perspective, position) item and column chunk, a few
+// consecutive items per warp.  The warp reads all index slots of an item at
+// once (8 coalesced loads of 32), compacts the valid ones into a per-warp
+// shared-memory list (ascending k) and walks it U rows at a time: all U x V
+// 128-bit row loads are issued before the U x V adds.  The next item's
+// indices are loaded while the current item's rows are in flight, so the
+// index latency is hidden.  Lanes own fixed column vectors, which keeps the
+// per-column add order.
 #pragma once
 
 #include "common.cuh"
@@ -30,10 +33,42 @@ struct FwdParams {
   Geom g;
 };
 
+constexpr int kIdxGroups = 8;  // index slots read per item in one go: 8 x 32 = 256
+
+// Loads slots [32 * g0, 32 * (g0 + kIdxGroups)) of one index row, one group of
+// 32 per register, all loads in flight together.
+__device__ __forceinline__ void load_index_groups(const int32_t* __restrict__ irow, int K, int g0, int lane,
+                                                  int (&f)[kIdxGroups]) {
+#pragma unroll
+  for (int g = 0; g < kIdxGroups; ++g) {
+    const int k = (g0 + g) * 32 + lane;
+    f[g] = k < K ? __ldcs(irow + k) : -1;
+  }
+}
+
+// Writes the valid indices of f[] (ascending slot order) to `list`; returns
+// how many.  Indices outside [-1, T) are flagged and dropped.
+__device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, int* list, int lane) {
+  const unsigned lt = lanemask_lt();
+  int n = 0;
+#pragma unroll
+  for (int g = 0; g < kIdxGroups; ++g) {
+    const bool valid = (unsigned)f[g] < (unsigned)T;
+    if (!valid && f[g] != -1) flag_error(kErrBadIndex);
+    const unsigned m = __ballot_sync(kFull, valid);
+    if (valid) list[n + __popc(m & lt)] = f[g];
+    n += __popc(m);
+  }
+  __syncwarp();
+  return n;
+}
+
 template <typename VT, int V, int U>
 __global__ void __launch_bounds__(kBlock) ft_forward_kernel(const FwdParams p) {
   using Ops = Vec<VT>;
+  __shared__ int s_list[kWarpsPerBlock][32 * kIdxGroups];
   const int lane = threadIdx.x & 31;
+  int* list = s_list[threadIdx.x >> 5];
   const int chunk = p.chunk0 + blockIdx.y;
   const int c0 = p.g.begin(chunk);
   const int width = p.g.width(chunk);
@@ -52,44 +87,60 @@ __global__ void __launch_bounds__(kBlock) ft_forward_kernel(const FwdParams p) {
   const int64_t n_items = (int64_t)p.P * p.B;
   int64_t item = ((int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5)) * p.items_per_warp;
   const int64_t item_end = item + p.items_per_warp < n_items ? item + p.items_per_warp : n_items;
+  if (item >= item_end) return;
+
+  auto index_row = [&](int64_t it) {
+    const int q = it >= p.B ? 1 : 0;
+    return (q ? p.idx[1] : p.idx[0]) + (it - (int64_t)q * p.B) * p.K;
+  };
+  const int n_super = (p.K + 32 * kIdxGroups - 1) / (32 * kIdxGroups);  // 1 for K <= 256
+
+  // indices of the first item; later items are prefetched one item ahead
+  int f[kIdxGroups];
+  load_index_groups(index_row(item), p.K, 0, lane, f);
 
   for (; item < item_end; ++item) {
     const int persp = item >= p.B ? 1 : 0;
     const int64_t b = item - (int64_t)persp * p.B;
-    const int32_t* __restrict__ irow = (persp ? p.idx[1] : p.idx[0]) + b * p.K;
+    const int32_t* __restrict__ irow = index_row(item);
 
     VT acc[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) acc[v] = bias_r[v];
 
-    for (int k0 = 0; k0 < p.K; k0 += 32) {
-      const int kk = k0 + lane;
-      const int f = kk < p.K ? __ldcs(irow + kk) : -1;
-      const bool valid = (unsigned)f < (unsigned)p.T;
-      if (!valid && f != -1) flag_error(kErrBadIndex);
-      unsigned mask = __ballot_sync(kFull, valid);
-      while (mask) {
-        int rows[U];
-        bool has[U];
+    for (int sg = 0; sg < n_super; ++sg) {
+      if (sg > 0) load_index_groups(irow, p.K, sg * kIdxGroups, lane, f);
+      const int n = compact_valid(f, p.T, list, lane);
+      // prefetch the next item's indices while this item's rows are in flight
+      if (sg == n_super - 1 && item + 1 < item_end) load_index_groups(index_row(item + 1), p.K, 0, lane, f);
+      // Two batches of U rows in flight: batch i + 1 is issued before batch
+      // i is added, so the warp never drains its loads between batches.
+      VT wa[U][V], wb[U][V];
+      int ra[U], rb[U];
+      auto fetch = [&](int u0, VT (&w)[U][V], int (&r)[U]) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          has[u] = mask != 0;
-          const int src = has[u] ? __ffs(mask) - 1 : 0;
-          rows[u] = __shfl_sync(kFull, f, src);
-          mask &= mask - 1;
+          r[u] = u0 + u < n ? list[u0 + u] : -1;
+#pragma unroll
+          for (int v = 0; v < V; ++v)
+            if (r[u] >= 0 && ok[v]) w[u][v] = Ops::ldg(Wv + (int64_t)r[u] * row_vec + 32 * v);
         }
-        VT w[U][V];
+      };
+      auto consume = [&](const VT (&w)[U][V], const int (&r)[U]) {
 #pragma unroll
         for (int u = 0; u < U; ++u)
 #pragma unroll
           for (int v = 0; v < V; ++v)
-            if (has[u] && ok[v]) w[u][v] = Ops::ldg(Wv + (int64_t)rows[u] * row_vec + 32 * v);
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-          for (int v = 0; v < V; ++v)
-            if (has[u] && ok[v]) Ops::add(acc[v], w[u][v]);
+            if (r[u] >= 0 && ok[v]) Ops::add(acc[v], w[u][v]);
+      };
+      if (n > 0) fetch(0, wa, ra);
+      for (int u0 = 0; u0 < n; u0 += 2 * U) {
+        if (u0 + U < n) fetch(u0 + U, wb, rb);
+        consume(wa, ra);
+        if (u0 + 2 * U < n) fetch(u0 + 2 * U, wa, ra);
+        if (u0 + U < n) consume(wb, rb);
       }
+      __syncwarp();  // every lane has read `list` before it is rewritten
     }
     VT* o = reinterpret_cast<VT*>(persp ? p.out[1] : p.out[0]) + b * row_vec + c0 + lane;
 #pragma unroll

@@ -46,14 +46,19 @@ int check_launch(const char* what) {
 }
 
 struct Tuning {
-  int64_t fwd_chunk_vec = 64;      // forward column chunk, in 16-byte vectors
-  int64_t fwd_items_per_warp = 4;  // (perspective, position) items per warp
+  int64_t fwd_chunk_vec = 53;       // forward column chunk, in 16-byte vectors
+  int64_t fwd_items_per_warp = 16;  // (perspective, position) items per warp
   int64_t fwd_unroll = 4;          // table rows in flight per warp (4 or 8)
   int64_t bwd_unroll = 4;          // dOut rows in flight per warp, light rows (4 or 8)
-  int64_t bwd_chunk_vec = 64;      // backward column chunk, in 16-byte vectors
+  int64_t bwd_entries_per_warp = 2048;  // streaming backward: sorted entries per warp
+  int64_t fwd_exact_chunks = 0;    // 1: full-width chunks + narrow tail; 0: balanced widths
+  int64_t bwd_exact_chunks = 1;
+  int64_t bwd_variant = 1;         // 1: per-row walk + heavy-row kernel, 0: streaming cp.async segment sums
+  int64_t bwd_stream_cfg = 0;      // streaming kernel shape (stages / group / warps per block)
+  int64_t bwd_chunk_vec = 32;      // backward column chunk, in 16-byte vectors
   int64_t heavy_threshold = 256;   // rows with more entries are split finer
   int64_t heavy_cap = 512;         // at most this many heavy rows per call
-  int64_t sort_tile_raw = 2048;    // raw index entries per warp in the first sort pass
+  int64_t sort_tile_rows = 32;     // index rows (positions) per warp in the first sort pass
   int64_t sort_tile = 1024;        // entries per warp in later sort passes
   int64_t colsum_parts = 296;      // position ranges of the bias column sum
 };
@@ -71,10 +76,15 @@ ParamRef* params() {
       {"fwd_items_per_warp", &g_tune.fwd_items_per_warp, 1, 1024},
       {"fwd_unroll", &g_tune.fwd_unroll, 4, 8},
       {"bwd_unroll", &g_tune.bwd_unroll, 4, 8},
+      {"bwd_entries_per_warp", &g_tune.bwd_entries_per_warp, 32, 1 << 24},
+      {"fwd_exact_chunks", &g_tune.fwd_exact_chunks, 0, 1},
+      {"bwd_exact_chunks", &g_tune.bwd_exact_chunks, 0, 1},
+      {"bwd_variant", &g_tune.bwd_variant, 0, 1},
+      {"bwd_stream_cfg", &g_tune.bwd_stream_cfg, 0, 5},
       {"bwd_chunk_vec", &g_tune.bwd_chunk_vec, 0, 1 << 20},
       {"heavy_threshold", &g_tune.heavy_threshold, 1, int64_t(1) << 40},
       {"heavy_cap", &g_tune.heavy_cap, 0, 1 << 24},
-      {"sort_tile_raw", &g_tune.sort_tile_raw, 32 * kSortBatch, 1 << 20},
+      {"sort_tile_rows", &g_tune.sort_tile_rows, 1, 1 << 16},
       {"sort_tile", &g_tune.sort_tile, 32 * kSortBatch, 1 << 20},
       {"colsum_parts", &g_tune.colsum_parts, 1, 1 << 16},
       {nullptr, nullptr, 0, 0},
@@ -86,33 +96,24 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Column geometry.  Chunks of `chunk` vectors (clamped to [8, 128]) with the
-// remainder folded into the last one, so no chunk is wider than 255 vectors
-// and a lane never needs more than 8 of them (the widest kernel instance).
-// `chunk` <= 0 asks for one chunk per row when the row has <= 256 vectors.
+// Column geometry: ceil(n_vec / chunk) balanced chunks, chunk clamped to
+// [8, 256] vectors, so a lane never needs more than 8 vectors (the widest
+// kernel instance).  `chunk` <= 0 asks for one chunk per row when the row
+// has <= 256 vectors.
 constexpr int kMaxLaneVectors = 8;
 
-Geom make_geom(int32_t n_vec, int64_t chunk) {
+Geom make_geom(int32_t n_vec, int64_t chunk, bool exact) {
   Geom g;
   g.n_vec = n_vec;
-  if ((chunk <= 0 || chunk >= n_vec) && n_vec <= 32 * kMaxLaneVectors) {
-    g.chunk_vec = n_vec;
-    g.n_chunks = 1;
-    g.last_vec = n_vec;
-    return g;
-  }
-  if (chunk <= 0) chunk = 128;
-  chunk = std::min<int64_t>(std::max<int64_t>(chunk, 8), 128);
-  g.chunk_vec = (int32_t)chunk;
-  g.n_chunks = (int32_t)std::max<int64_t>(1, n_vec / chunk);
-  g.last_vec = n_vec - (g.n_chunks - 1) * g.chunk_vec;
+  if (chunk <= 0) chunk = 32 * kMaxLaneVectors;
+  chunk = std::min<int64_t>(std::max<int64_t>(chunk, 8), 32 * kMaxLaneVectors);
+  g.n_chunks = (int32_t)std::max<int64_t>(1, ceil_div(n_vec, chunk));
+  g.exact = exact ? 1 : 0;
+  g.max_width = exact ? (int32_t)std::min<int64_t>(chunk, n_vec) : (int32_t)ceil_div(n_vec, g.n_chunks);
   return g;
 }
 
-int lanes_per_row(const Geom& g) {  // vectors per lane needed by the widest chunk
-  const int w = std::max(g.n_chunks > 1 ? g.chunk_vec : 0, g.last_vec);
-  return (w + 31) / 32;
-}
+int lanes_per_row(const Geom& g) { return (g.max_width + 31) / 32; }
 
 // ---------------------------------------------------------------------------
 // forward
@@ -129,9 +130,14 @@ void launch_forward_vu(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
 
 template <typename VT, int V>
 void launch_forward_v(const FwdParams& p, int chunk0, int n_chunks, cudaStream_t s) {
-  if (V <= 2 && g_tune.fwd_unroll >= 8) launch_forward_vu<VT, V, 8>(p, chunk0, n_chunks, s);
-  else if (V <= 4) launch_forward_vu<VT, V, 4>(p, chunk0, n_chunks, s);
-  else launch_forward_vu<VT, V, 2>(p, chunk0, n_chunks, s);
+  if constexpr (V <= 2) {
+    if (g_tune.fwd_unroll >= 8) launch_forward_vu<VT, V, 8>(p, chunk0, n_chunks, s);
+    else launch_forward_vu<VT, V, 4>(p, chunk0, n_chunks, s);
+  } else if constexpr (V <= 4) {
+    launch_forward_vu<VT, V, 4>(p, chunk0, n_chunks, s);
+  } else {
+    launch_forward_vu<VT, V, 2>(p, chunk0, n_chunks, s);
+  }
 }
 
 template <typename VT>
@@ -145,12 +151,9 @@ void launch_forward_range(const FwdParams& p, int chunk0, int n_chunks, int widt
   }
 }
 
-// Chunks [0, n-1) share one width; the last (wider) chunk gets its own launch
-// so each launch is compiled for exactly the vectors per lane it needs.
 template <typename VT>
 void launch_forward(const FwdParams& p, cudaStream_t s) {
-  if (p.g.n_chunks > 1) launch_forward_range<VT>(p, 0, p.g.n_chunks - 1, p.g.chunk_vec, s);
-  launch_forward_range<VT>(p, p.g.n_chunks - 1, 1, p.g.last_vec, s);
+  launch_forward_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
 }
 
 int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int32_t K, const float* W,
@@ -174,7 +177,8 @@ int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int
   p.T = (int32_t)T;
   p.P = P;
   p.items_per_warp = (int32_t)g_tune.fwd_items_per_warp;
-  p.g = v4 ? make_geom(C / 4, g_tune.fwd_chunk_vec) : make_geom(C, g_tune.fwd_chunk_vec * 4);
+  p.g = v4 ? make_geom(C / 4, g_tune.fwd_chunk_vec, g_tune.fwd_exact_chunks)
+             : make_geom(C, g_tune.fwd_chunk_vec * 4, g_tune.fwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "forward: column chunk too wide");
   if (v4) launch_forward<float4>(p, s);
   else launch_forward<float>(p, s);
@@ -190,9 +194,9 @@ struct BwdPlan {
   int bits = 0, npass = 0;
   int dbits[3] = {0, 0, 0}, shift[3] = {0, 0, 0};
   int64_t tile_raw = 0, tile = 0, tiles_raw = 0, tiles_max = 0, hist_len = 0, scan_blocks = 0;
-  int64_t heavy_cap = 0, heavy_threshold = 0, parts = 0;
+  int64_t heavy_cap = 0, heavy_threshold = 0, parts = 0, epw = 0, n_stream_warps = 0;
   size_t off_seg = 0, off_hist = 0, off_bsum = 0, off_ka = 0, off_va = 0, off_kb = 0, off_vb = 0;
-  size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, total = 0;
+  size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, off_first = 0, total = 0;
 };
 
 int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl) {
@@ -218,9 +222,9 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
     pl.shift[i] = sh;
     sh += d;
   }
-  pl.tile_raw = g_tune.sort_tile_raw / (32 * kSortBatch) * (32 * kSortBatch);
+  pl.tile_raw = g_tune.sort_tile_rows;  // rows per warp tile in the first pass
   pl.tile = g_tune.sort_tile / (32 * kSortBatch) * (32 * kSortBatch);
-  pl.tiles_raw = ceil_div(pl.nnz_max, pl.tile_raw);
+  pl.tiles_raw = pl.K > 0 ? ceil_div((int64_t)P * B, pl.tile_raw) : 0;
   pl.tiles_max = ceil_div(pl.nnz_max, pl.tile);
   pl.hist_len = (int64_t(1) << pl.dbits[0]) * pl.tiles_raw;
   for (int i = 1; i < pl.npass; ++i)
@@ -229,6 +233,8 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
   pl.heavy_cap = std::min<int64_t>(g_tune.heavy_cap, T);
   pl.heavy_threshold = g_tune.heavy_threshold;
   pl.parts = std::max<int64_t>(1, std::min<int64_t>(g_tune.colsum_parts, B));
+  pl.epw = g_tune.bwd_entries_per_warp;
+  pl.n_stream_warps = pl.nnz_max / pl.epw + 1;
   const int64_t n_vec_floats = C;  // float64 partial column sums
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -247,6 +253,7 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
   pl.off_heavy = take(sizeof(int32_t) * pl.heavy_cap);
   pl.off_kind = take(sizeof(uint8_t) * T);
   pl.off_partial = take(sizeof(double) * P * pl.parts * n_vec_floats);
+  pl.off_first = take(sizeof(int32_t) * (pl.n_stream_warps + 1));
   pl.total = o;
   return NNUE_OK;
 }
@@ -255,6 +262,7 @@ struct Ws {
   int32_t *seg, *hist, *bsum, *ka, *va, *kb, *vb, *nheavy, *heavy;
   uint8_t* kind;
   double* partial;
+  int32_t* first_row;
 };
 
 Ws carve(const BwdPlan& pl, void* base) {
@@ -271,6 +279,7 @@ Ws carve(const BwdPlan& pl, void* base) {
   w.heavy = reinterpret_cast<int32_t*>(b + pl.off_heavy);
   w.kind = reinterpret_cast<uint8_t*>(b + pl.off_kind);
   w.partial = reinterpret_cast<double*>(b + pl.off_partial);
+  w.first_row = reinterpret_cast<int32_t*>(b + pl.off_first);
   return w;
 }
 
@@ -303,7 +312,6 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
     const bool first = i == 0, last = i == pl.npass - 1;
     PassParams pp{};
     pp.raw = raw;
-    pp.n_src = pl.nnz_max;
     pp.count = w.seg + pl.NK;  // number of valid entries, known after pass 0's scan
     pp.shift = pl.shift[i];
     pp.bits = pl.dbits[i];
@@ -325,17 +333,17 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
     const unsigned grid = (unsigned)ceil_div(tiles, kWarpsPerBlock);
     if (first) {
       count_launch();
-      sort_hist_kernel<true><<<grid, kBlock, smem, s>>>(pp);
+      sort_hist_rows_kernel<<<grid, kBlock, smem, s>>>(pp);
       run_scan(w.hist, ScanLen{bins * tiles, nullptr, 0, 0}, bins * tiles, w.bsum, s);
       run_scan(w.seg, ScanLen{pl.NK + 1, nullptr, 0, 0}, pl.NK + 1, w.bsum, s);
       count_launch();
-      sort_scatter_kernel<true><<<grid, kBlock, smem, s>>>(pp);
+      sort_scatter_rows_kernel<<<grid, kBlock, smem, s>>>(pp);
     } else {
       count_launch();
-      sort_hist_kernel<false><<<grid, kBlock, smem, s>>>(pp);
+      sort_hist_kernel<<<grid, kBlock, smem, s>>>(pp);
       run_scan(w.hist, ScanLen{0, pp.count, pp.tile, bins}, (int64_t)bins * tiles, w.bsum, s);
       count_launch();
-      sort_scatter_kernel<false><<<grid, kBlock, smem, s>>>(pp);
+      sort_scatter_kernel<<<grid, kBlock, smem, s>>>(pp);
     }
   }
   if (pl.nnz_max == 0) {
@@ -345,22 +353,30 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
   classify_rows_kernel<<<(unsigned)ceil_div(pl.T, kBlock), kBlock, 0, s>>>(
       w.seg, (int32_t)pl.T, pl.P, (int32_t)std::min<int64_t>(pl.heavy_threshold, INT32_MAX),
       (int32_t)pl.heavy_cap, w.nheavy, w.heavy, w.kind);
+  count_launch();
+  warp_ranges_kernel<<<(unsigned)ceil_div(pl.T + 1, kBlock), kBlock, 0, s>>>(
+      w.seg, (int32_t)pl.T, pl.P, (int32_t)pl.epw, (int32_t)pl.n_stream_warps, w.first_row);
   return check_launch("backward_prepare");
 }
 
 template <typename VT, int V, int U>
 void launch_segsum_vu(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
-  dim3 grid((unsigned)ceil_div(p.T, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
-  ft_segsum_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
+  dim3 grid((unsigned)ceil_div(p.T, kWarpsPerBlock), (unsigned)n_chunks);
+  ft_segsum_walk_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
 }
 
 template <typename VT, int V>
 void launch_segsum_v(const SegParams& p, int chunk0, int n_chunks, cudaStream_t s) {
-  if (V <= 2 && g_tune.bwd_unroll >= 8) launch_segsum_vu<VT, V, 8>(p, chunk0, n_chunks, s);
-  else if (V <= 4) launch_segsum_vu<VT, V, 4>(p, chunk0, n_chunks, s);
-  else launch_segsum_vu<VT, V, 2>(p, chunk0, n_chunks, s);
+  if constexpr (V <= 2) {
+    if (g_tune.bwd_unroll >= 8) launch_segsum_vu<VT, V, 8>(p, chunk0, n_chunks, s);
+    else launch_segsum_vu<VT, V, 4>(p, chunk0, n_chunks, s);
+  } else if constexpr (V <= 4) {
+    launch_segsum_vu<VT, V, 4>(p, chunk0, n_chunks, s);
+  } else {
+    launch_segsum_vu<VT, V, 2>(p, chunk0, n_chunks, s);
+  }
 }
 
 template <typename VT>
@@ -376,8 +392,7 @@ void launch_segsum_range(const SegParams& p, int chunk0, int n_chunks, int width
 
 template <typename VT>
 void launch_segsum_light(const SegParams& p, cudaStream_t s) {
-  if (p.g.n_chunks > 1) launch_segsum_range<VT>(p, 0, p.g.n_chunks - 1, p.g.chunk_vec, s);
-  launch_segsum_range<VT>(p, p.g.n_chunks - 1, 1, p.g.last_vec, s);
+  launch_segsum_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
 }
 
 template <typename VT>
@@ -446,6 +461,38 @@ void launch_colsum(const float* g0, const float* g1, const BwdPlan& pl, bool vec
                                                                                  pl.C, dB, accumulate);
 }
 
+template <int SV, int S, int G, int WPB>
+int launch_segsum_stream_cfg(SegParams p, cudaStream_t s) {
+  constexpr size_t smem = sizeof(float4) * 32 * SV * S * WPB;
+  static std::atomic<unsigned long long> attr_set_mask{0};  // one bit per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("backward_apply: device");
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (smem > 48 * 1024 && !(attr_set_mask.load() & bit)) {
+    if (cudaFuncSetAttribute(ft_segsum_stream_kernel<SV, S, G, WPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return check_launch("backward_apply: stream kernel shared memory");
+    attr_set_mask.fetch_or(bit);
+  }
+  p.chunk0 = 0;
+  dim3 grid((unsigned)ceil_div(p.n_stream_warps, WPB), (unsigned)p.g.n_chunks);
+  count_launch();
+  ft_segsum_stream_kernel<SV, S, G, WPB><<<grid, 32 * WPB, smem, s>>>(p);
+  return NNUE_OK;
+}
+
+template <int SV>
+int launch_segsum_stream(const SegParams& p, cudaStream_t s) {
+  switch (g_tune.bwd_stream_cfg) {
+    case 0: return launch_segsum_stream_cfg<SV, 16, 4, 4>(p, s);
+    case 1: return launch_segsum_stream_cfg<SV, 16, 4, 8>(p, s);
+    case 2: return launch_segsum_stream_cfg<SV, 8, 2, 8>(p, s);
+    case 3: return launch_segsum_stream_cfg<SV, 32, 4, 4>(p, s);
+    case 4: return launch_segsum_stream_cfg<SV, 16, 1, 4>(p, s);
+    default: return launch_segsum_stream_cfg<SV, 8, 4, 8>(p, s);
+  }
+}
+
 int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w, float* dW, float* dB,
                int32_t accumulate, cudaStream_t s) {
   const bool v4 = (pl.C % 4 == 0) && aligned16(g0) && (pl.P == 1 || aligned16(g1)) && aligned16(dW) &&
@@ -464,24 +511,36 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   p.P = pl.P;
   p.accumulate = accumulate ? 1 : 0;
   p.heavy_cap = (int32_t)pl.heavy_cap;
-  p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec) : make_geom(pl.C, g_tune.bwd_chunk_vec * 4);
+  p.first_row = w.first_row;
+  p.n_stream_warps = (int32_t)pl.n_stream_warps;
+  p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec, g_tune.bwd_exact_chunks)
+             : make_geom(pl.C, g_tune.bwd_chunk_vec * 4, g_tune.bwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "backward: column chunk too wide");
 
+  const bool stream = v4 && g_tune.bwd_variant == 0 && lanes_per_row(p.g) <= 2;
   DeviceAux* aux = nullptr;
   int rc = device_aux(&aux);
   if (rc != NNUE_OK) return rc;
   {
-    // fork: heavy rows + bias column sum on the side stream
+    // fork: (fallback path: heavy rows +) bias column sum on the side stream
     std::lock_guard<std::mutex> lock(g_aux_mu);
     if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
       return check_launch("backward_apply: fork");
-    rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
-    if (rc != NNUE_OK) return rc;
+    if (!stream) {
+      rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
+      if (rc != NNUE_OK) return rc;
+    }
     launch_colsum(g0, g1, pl, v4, w.partial, dB, p.accumulate, aux->side);
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
   }
-  if (v4) launch_segsum_light<float4>(p, s);
-  else launch_segsum_light<float>(p, s);
+  if (stream) {
+    rc = lanes_per_row(p.g) == 1 ? launch_segsum_stream<1>(p, s) : launch_segsum_stream<2>(p, s);
+    if (rc != NNUE_OK) return rc;
+  } else if (v4) {
+    launch_segsum_light<float4>(p, s);
+  } else {
+    launch_segsum_light<float>(p, s);
+  }
   // A later record of `join` by another call is further down the same
   // in-order side stream, so waiting on it also covers this call's work.
   if (cudaStreamWaitEvent(s, aux->join, 0) != cudaSuccess) return check_launch("backward_apply: join");
@@ -569,6 +628,34 @@ int nnue_ft_forward_pair(const int32_t* idx0, const int32_t* idx1, int64_t batch
                          float* out1, void* stream) {
   return forward_impl(idx0, idx1, 2, batch, max_active, weight, num_inputs, output_size, bias, out0, out1,
                       static_cast<cudaStream_t>(stream));
+}
+
+int nnue_ft_forward_pair_prepare(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active,
+                                 const float* weight, int64_t num_inputs, int32_t output_size, const float* bias,
+                                 float* out0, float* out1, void* workspace, size_t workspace_bytes, void* stream) {
+  BwdPlan pl;
+  int rc = make_plan(batch, max_active, num_inputs, output_size, 2, pl);
+  if (rc != NNUE_OK) return rc;
+  rc = check_bwd_args(idx0, idx1, 2, workspace, workspace_bytes, pl);
+  if (rc != NNUE_OK) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceAux* aux = nullptr;
+  rc = device_aux(&aux);
+  if (rc != NNUE_OK) return rc;
+  {
+    // the backward's index-only phase runs on the side stream, concurrently
+    // with the forward gather on the caller's stream
+    std::lock_guard<std::mutex> lock(g_aux_mu);
+    if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
+      return check_launch("forward_pair_prepare: fork");
+    rc = prepare_impl(idx0, idx1, pl, carve(pl, workspace), aux->side);
+    if (rc != NNUE_OK) return rc;
+    if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("forward_pair_prepare: join record");
+  }
+  rc = forward_impl(idx0, idx1, 2, batch, max_active, weight, num_inputs, output_size, bias, out0, out1, s);
+  if (rc != NNUE_OK) return rc;
+  if (cudaStreamWaitEvent(s, aux->join, 0) != cudaSuccess) return check_launch("forward_pair_prepare: join");
+  return NNUE_OK;
 }
 
 size_t nnue_ft_backward_workspace_size(int64_t batch, int32_t max_active, int64_t num_inputs, int32_t output_size,

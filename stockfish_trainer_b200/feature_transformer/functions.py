@@ -75,11 +75,24 @@ class SparseLinearFunction(autograd.Function):
 
 @torch.compiler.disable
 def _forward_pair(idx0, idx1, weight, bias):
-    B = idx0.shape[0]
-    out0 = torch.empty(B, weight.shape[1], dtype=torch.float32, device=idx0.device)
+    B, K = idx0.shape
+    T, C = weight.shape
+    out0 = torch.empty(B, C, dtype=torch.float32, device=idx0.device)
     out1 = torch.empty_like(out0)
-    ops.forward_pair_into(idx0, idx1, weight, bias, out0, out1)
-    return out0, out1
+    # The backward's index-only phase (sorted position lists per feature) runs
+    # during the forward, on the library's side stream; its workspace lives
+    # until the backward consumes it.
+    ws = ops.alloc_workspace(B, K, T, C, 2, idx0.device)
+    ops.forward_pair_prepare(idx0, idx1, weight, bias, out0, out1, ws)
+    return out0, out1, ws
+
+
+@torch.compiler.disable
+def _backward_pair_apply(grad0, grad1, batch, max_active, num_inputs, output_size, ws):
+    weight_grad = torch.empty(num_inputs, output_size, dtype=torch.float32, device=grad0.device)
+    bias_grad = torch.empty(output_size, dtype=torch.float32, device=grad0.device)
+    ops.backward_apply(grad0, grad1, batch, max_active, weight_grad, bias_grad, False, ws)
+    return weight_grad, bias_grad
 
 
 class SparseLinearPairFunction(autograd.Function):
@@ -91,13 +104,17 @@ class SparseLinearPairFunction(autograd.Function):
         _check_inputs(feature_indices_1, weight, bias)
         assert feature_indices_0.shape == feature_indices_1.shape
         ctx.save_for_backward(feature_indices_0, feature_indices_1, weight)
-        return _forward_pair(feature_indices_0, feature_indices_1, weight, bias)
+        out0, out1, ws = _forward_pair(feature_indices_0, feature_indices_1, weight, bias)
+        ctx.workspace = ws
+        return out0, out1
 
     @staticmethod
     def backward(ctx, grad0, grad1):
         assert not ctx.needs_input_grad[0] and not ctx.needs_input_grad[1]
         idx0, idx1, weight = ctx.saved_tensors
+        ws, ctx.workspace = ctx.workspace, None
         T, C = weight.shape
+        B, K = idx0.shape
         if grad0 is None and grad1 is None:
             return None, None, None, None
         if grad0 is None:
@@ -105,5 +122,5 @@ class SparseLinearPairFunction(autograd.Function):
         elif grad1 is None:
             weight_grad, bias_grad = _backward(idx0, None, grad0.contiguous(), None, T, C)
         else:
-            weight_grad, bias_grad = _backward(idx0, idx1, grad0.contiguous(), grad1.contiguous(), T, C)
+            weight_grad, bias_grad = _backward_pair_apply(grad0.contiguous(), grad1.contiguous(), B, K, T, C, ws)
         return None, None, weight_grad, bias_grad

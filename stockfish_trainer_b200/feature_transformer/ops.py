@@ -68,6 +68,29 @@ def forward_pair_into(idx0, idx1, weight, bias, out0, out1) -> None:
                      bias.data_ptr(), out0.data_ptr(), out1.data_ptr(), _stream_ptr(dev))
 
 
+def forward_pair_prepare(idx0, idx1, weight, bias, out0, out1, workspace: torch.Tensor) -> None:
+    """forward_pair_into + backward_prepare (two perspectives) in one call: the
+    index-only backward phase runs on the library's side stream while the
+    forward gathers, and the current stream waits for both."""
+    _check(idx0, "feature_indices_0", torch.int32, 2)
+    dev = idx0.device
+    _check(idx1, "feature_indices_1", torch.int32, 2, dev)
+    _check(weight, "weight", torch.float32, 2, dev)
+    _check(bias, "bias", torch.float32, 1, dev)
+    _check(out0, "output_0", torch.float32, 2, dev)
+    _check(out1, "output_1", torch.float32, 2, dev)
+    if idx0.shape != idx1.shape:
+        raise ValueError("both perspectives need the same [batch, max_active] shape")
+    B, K = idx0.shape
+    T, C = weight.shape
+    if bias.shape[0] != C or tuple(out0.shape) != (B, C) or tuple(out1.shape) != (B, C):
+        raise ValueError("bias / output shapes do not match weight and indices")
+    with torch.cuda.device(dev):
+        _native.call("nnue_ft_forward_pair_prepare", idx0.data_ptr(), idx1.data_ptr(), B, K, weight.data_ptr(), T, C,
+                     bias.data_ptr(), out0.data_ptr(), out1.data_ptr(), workspace.data_ptr(), workspace.numel(),
+                     _stream_ptr(dev))
+
+
 def workspace_bytes(batch: int, max_active: int, num_inputs: int, output_size: int, n_persp: int) -> int:
     n = int(_native.load().nnue_ft_backward_workspace_size(batch, max_active, num_inputs, output_size, n_persp))
     if n == 0:

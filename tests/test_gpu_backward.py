@@ -84,14 +84,22 @@ def _with_params(params, fn):
 @pytest.mark.parametrize(
     "params",
     [
-        {"heavy_threshold": 4, "heavy_cap": 3},  # some heavy rows overflow to the light path
-        {"heavy_threshold": 1, "heavy_cap": 100000},  # nearly every row heavy
-        {"heavy_threshold": 10**9},  # no heavy rows
+        {"bwd_variant": 1, "heavy_threshold": 4, "heavy_cap": 3},  # heavy rows overflow to the light path
+        {"bwd_variant": 1, "heavy_threshold": 1, "heavy_cap": 100000},  # nearly every row heavy
+        {"bwd_variant": 1, "heavy_threshold": 10**9},  # no heavy rows
+        {"bwd_variant": 1},
+        {"bwd_entries_per_warp": 32},
+        {"bwd_entries_per_warp": 100},
+        {"bwd_entries_per_warp": 5000},
+        {"bwd_exact_chunks": 1},
+        {"bwd_chunk_vec": 64, "bwd_exact_chunks": 1},
+        {"bwd_chunk_vec": 8},
         {"bwd_chunk_vec": 0},
         {"bwd_chunk_vec": 32},
         {"bwd_chunk_vec": 128},
         {"bwd_chunk_vec": 1000},
-        {"sort_tile_raw": 512, "sort_tile": 512},
+        {"sort_tile_rows": 1, "sort_tile": 512},
+        {"sort_tile_rows": 7, "sort_tile": 1536},
         {"colsum_parts": 1},
     ],
 )
@@ -183,3 +191,27 @@ def test_backward_workspace_too_small_raises(cuda):
     ws = torch.empty(64, dtype=torch.uint8, device=cuda)
     with pytest.raises(_native.NativeError):
         ops.backward_prepare(idx, None, T, C, ws)
+
+
+def test_forward_pair_prepare_then_apply(cuda):
+    """The fused forward + concurrent index phase feeds apply exactly like the
+    separate calls."""
+    white, black, T = feature_batch(1500, "Full_Threats+HalfKAv2_hm^", seed=71)
+    B, C, K = 1500, 1048, white.shape[1]
+    rng = np.random.default_rng(72)
+    W = torch.from_numpy(rng.standard_normal((T, C), dtype=np.float32) * np.float32(0.01)).to(cuda)
+    bias = torch.zeros(C, device=cuda)
+    g0, g1 = _grads(B, C, 73)
+    i0, i1 = torch.from_numpy(white).to(cuda), torch.from_numpy(black).to(cuda)
+    o0 = torch.empty(B, C, device=cuda)
+    o1 = torch.empty_like(o0)
+    ws = ops.alloc_workspace(B, K, T, C, 2, cuda)
+    ops.forward_pair_prepare(i0, i1, W, bias, o0, o1, ws)
+    dW = torch.empty(T, C, device=cuda)
+    dB = torch.empty(C, device=cuda)
+    ops.backward_apply(torch.from_numpy(g0).to(cuda), torch.from_numpy(g1).to(cuda), B, K, dW, dB, False, ws)
+    Wn = W.cpu().numpy()
+    np.testing.assert_array_equal(o0.cpu().numpy(), oracle.ft_forward(white, Wn, bias.cpu().numpy()))
+    rW, rB = oracle.ft_backward_pair(white, black, g0, g1, T)
+    np.testing.assert_array_equal(dW.cpu().numpy(), rW)
+    np.testing.assert_allclose(dB.cpu().numpy(), rB, rtol=RTOL, atol=ATOL)

@@ -130,6 +130,33 @@ int nnue_ft_forward_pair_prepare(const int32_t *idx0, const int32_t *idx1, int64
                                  const float *weight, int64_t num_inputs, int32_t output_size, const float *bias,
                                  float *out0, float *out1, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Backward for callers that cannot allocate device memory: the same result
+ * as nnue_ft_backward (same arguments minus the workspace), with its scratch
+ * taken from a fixed 16 MiB device array inside this library instead of a
+ * caller workspace.  It has no counterpart in the reference.
+ *   - Who needs it: code that must not call cudaMalloc or an allocator per
+ *     call, e.g. a search / inference loop on a fixed memory budget, or a
+ *     host that reaches the GPU only through this C ABI with tensors owned by
+ *     someone else and no way to provide a workspace.
+ *   - Limit: sizes whose nnue_ft_backward_workspace_size() exceeds
+ *     nnue_ft_noalloc_scratch_bytes() are rejected with NNUE_ERR_UNSUPPORTED
+ *     (HalfKAv2_hm, C = 1048: about 8K positions; Full_Threats+HalfKAv2_hm:
+ *     a few thousand).
+ *   - The array exists on every GPU that loads the library until the process
+ *     exits.  The first call on each device looks up its device address
+ *     (and, like nnue_ft_backward, creates the library's side stream); make
+ *     that first call before any stream capture.
+ *   - All calls share the one array and it keeps the previous call's
+ *     contents (everything that must start at zero is cleared by each call).
+ *     Calls that overlap on the GPU (different streams, or other threads)
+ *     race on it: serialise them. */
+int nnue_ft_backward_noalloc(const int32_t *idx0, const int32_t *idx1, int64_t batch, int32_t max_active,
+                             const float *grad0, const float *grad1, int32_t n_persp, int64_t num_inputs,
+                             int32_t output_size, float *weight_grad, float *bias_grad, int32_t accumulate,
+                             void *stream);
+/* Size of that fixed scratch array, in bytes. */
+size_t nnue_ft_noalloc_scratch_bytes(void);
+
 /* ---- quantised (int16) forward ------------------------------------------
  * The inference forward of a serialised net (the engine's accumulator
  * refresh; the engine is not part of the reference):

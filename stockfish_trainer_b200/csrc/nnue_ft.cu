@@ -572,6 +572,39 @@ void launch_qforward_v(const QFwdParams& p, cudaStream_t s) {
 }  // namespace
 }  // namespace nnue
 
+// ---------------------------------------------------------------------------
+// Scratch for nnue_ft_backward_noalloc: a fixed device array that exists on
+// every GPU that loads this library, for as long as the process lives.  Host
+// code must not pass the symbol itself to a kernel (on the host it is only a
+// stand-in); its device address comes from cudaGetSymbolAddress, looked up
+// once per device with that device current.
+// ---------------------------------------------------------------------------
+static constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace nnue {
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("backward_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(NNUE_ERR_UNSUPPORTED, "backward_noalloc: device ordinal %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(NNUE_ERR_CUDA, "backward_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return NNUE_OK;
+}
+}  // namespace
+}  // namespace nnue
+
 using namespace nnue;
 
 extern "C" {
@@ -775,6 +808,27 @@ int nnue_ft_quantize_i16(const float* x, int64_t n, float scale, int16_t* q, voi
   count_launch();
   quantize_i16_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, scale, q);
   return check_launch("quantize_i16");
+}
+
+size_t nnue_ft_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int nnue_ft_backward_noalloc(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active,
+                             const float* grad0, const float* grad1, int32_t n_persp, int64_t num_inputs,
+                             int32_t output_size, float* weight_grad, float* bias_grad, int32_t accumulate,
+                             void* stream) {
+  BwdPlan pl;
+  int rc = make_plan(batch, max_active, num_inputs, output_size, n_persp, pl);
+  if (rc != NNUE_OK) return rc;
+  if (pl.total > kNoAllocScratchBytes)
+    return fail(NNUE_ERR_UNSUPPORTED,
+                "backward_noalloc: these sizes need %zu bytes of scratch but the library's fixed scratch holds %zu; "
+                "use nnue_ft_backward with a caller workspace",
+                pl.total, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  rc = noalloc_scratch_address(&scratch);
+  if (rc != NNUE_OK) return rc;
+  return nnue_ft_backward(idx0, idx1, batch, max_active, grad0, grad1, n_persp, num_inputs, output_size, weight_grad,
+                          bias_grad, accumulate, scratch, kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"

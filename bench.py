@@ -61,6 +61,9 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--serial-prepare", action="store_true",
                    help="run the backward's index phase after the forward instead of concurrently with it")
+    p.add_argument("--ddp-blocks", type=int, default=4,
+                   help="N > 1: row blocks whose gradient allreduce overlaps the next block's backward "
+                        "(0 = one allreduce after the whole backward)")
     p.add_argument("--param", action="append", default=[], metavar="NAME=VALUE",
                    help="native tuning knob (see include/nnue_ft.h nnue_ft_set_param)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline time budget")
@@ -134,9 +137,19 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference path, all host threads)
 # ---------------------------------------------------------------------------
+def host_threads() -> int:
+    """All cores this process may run on (torchrun sets OMP_NUM_THREADS=1,
+    which must not throttle the CPU baseline)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(white, black, W_np, seed, budget_s, per_step=None):
     import oracle
 
+    nt = host_threads()
     T = W_np.shape[0]
     n = min(len(white), per_step or 4096)
     rng = np.random.default_rng(seed + 99)
@@ -148,9 +161,9 @@ def cpu_baseline(white, black, W_np, seed, budget_s, per_step=None):
     t_start = time.perf_counter()
     while True:
         t0 = time.perf_counter()
-        oracle.ft_forward(w, W_np, bias)
-        oracle.ft_forward(b, W_np, bias)
-        oracle.ft_backward_pair(w, b, g0, g1, T)
+        oracle.ft_forward(w, W_np, bias, nthreads=nt)
+        oracle.ft_forward(b, W_np, bias, nthreads=nt)
+        oracle.ft_backward_pair(w, b, g0, g1, T, nthreads=nt)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() - t_start > budget_s or len(times) >= 10:
             break
@@ -158,7 +171,7 @@ def cpu_baseline(white, black, W_np, seed, budget_s, per_step=None):
     return {
         "value": n / t_med,
         "unit": "positions/s",
-        "cores": oracle.max_threads(),
+        "cores": nt,
         "kind": "port",
         "sample": f"{n} positions of the headline workload (both perspectives, fwd + bwd incl. the two dense "
                   f"dW the reference allocates), median of {len(times)} reps, C oracle with OpenMP",
@@ -206,10 +219,12 @@ def run_reference(args):
     g1 = rng.standard_normal((n, C), dtype=np.float32)
     bias = np.zeros(C, np.float32)
 
+    nt = host_threads()
+
     def sample_step():
-        oracle.ft_forward(white, W_np, bias)
-        oracle.ft_forward(black, W_np, bias)
-        oracle.ft_backward_pair(white, black, g0, g1, T)
+        oracle.ft_forward(white, W_np, bias, nthreads=nt)
+        oracle.ft_forward(black, W_np, bias, nthreads=nt)
+        oracle.ft_backward_pair(white, black, g0, g1, T, nthreads=nt)
 
     for _ in range(args.warmup):
         sample_step()
@@ -235,12 +250,12 @@ def run_reference(args):
         "dtype": "f32",
         "data": DATA,
         "config": base_config(args, world, args.batch // max(world, 1), T, K),
-        "cpu_baseline": {"value": value, "unit": "positions/s", "cores": oracle.max_threads(), "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "positions/s", "cores": nt, "kind": "port",
                          "sample": f"each step: {n} positions of the headline workload, fwd + bwd of both "
                                    "perspectives (C restatement of the reference kernels, OpenMP)"},
         "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -300,12 +315,19 @@ def run_ours(args):
                 e[1].record()
         if e:
             e[2].record()
-        ops.backward_apply(g0, g1, b_rank, K, grads.weight, grads.bias, False, ws)
-        if e:
-            e[3].record()
-        grads.allreduce_mean(world)
-        if e:
-            e[4].record()
+        if world > 1 and args.ddp_blocks > 0:
+            # segment sums in row blocks, each block's allreduce overlapped with the next block
+            ddp.backward_allreduce_overlapped(g0, g1, b_rank, K, grads, ws, world, n_blocks=args.ddp_blocks)
+            if e:
+                e[3].record()
+                e[4].record()
+        else:
+            ops.backward_apply(g0, g1, b_rank, K, grads.weight, grads.bias, False, ws)
+            if e:
+                e[3].record()
+            grads.allreduce_mean(world)
+            if e:
+                e[4].record()
 
     def barrier():
         if world > 1:
@@ -340,6 +362,7 @@ def run_ours(args):
     launches = _native.launch_count() - l0
     ms_local = start.elapsed_time(end)
     ms = max_over_ranks(ms_local)
+    # with --ddp-blocks the "backward_apply" phase includes the overlapped allreduce
     phases = {
         ("forward" if args.serial_prepare else "forward+prepare"): [e[0].elapsed_time(e[1]) for e in ev[: args.steps]],
         "backward_prepare": [e[1].elapsed_time(e[2]) for e in ev[: args.steps]],
@@ -444,15 +467,34 @@ def run_ours(args):
             "clocks": clock_info,
             "gpu": torch.cuda.get_device_name(dev),
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
 
 
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    """Writes the one JSON result line to the real stdout."""
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
+
 def main():
+    global _JSON_FD
     args = parse_args()
+    # Libraries (NCCL, torch) may print banners on stdout; route all of that
+    # to stderr so stdout carries exactly one JSON line.
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

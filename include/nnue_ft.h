@@ -121,6 +121,15 @@ int nnue_ft_backward_apply(const float *grad0, const float *grad1, int64_t batch
                            float *bias_grad, int32_t accumulate, void *workspace, size_t workspace_bytes,
                            void *stream);
 
+/* nnue_ft_backward_apply restricted to weight-gradient rows [row_begin,
+ * row_end); the bias gradient is produced only when with_bias != 0 (bias_grad
+ * may then be null otherwise).  Lets a data-parallel caller start reducing
+ * finished rows while later rows are still being computed. */
+int nnue_ft_backward_apply_rows(const float *grad0, const float *grad1, int64_t batch, int32_t max_active,
+                                int32_t n_persp, int64_t num_inputs, int32_t output_size, float *weight_grad,
+                                float *bias_grad, int32_t accumulate, int64_t row_begin, int64_t row_end,
+                                int32_t with_bias, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Forward of both perspectives (nnue_ft_forward_pair) plus, concurrently on
  * the library's side stream, the index-only backward phase
  * (nnue_ft_backward_prepare with n_persp = 2) into `workspace`.  The caller's

@@ -40,6 +40,8 @@ _SIGNATURES = {
     "nnue_ft_forward_pair_prepare": (_I32, [_P, _P, _I64, _I32, _P, _I64, _I32, _P, _P, _P, _P, _SZ, _P]),
     "nnue_ft_backward_workspace_size": (_SZ, [_I64, _I32, _I64, _I32, _I32]),
     "nnue_ft_backward": (_I32, [_P, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I32, _P, _SZ, _P]),
+    "nnue_ft_backward_apply_rows": (
+        _I32, [_P, _P, _I64, _I32, _I32, _I64, _I32, _P, _P, _I32, _I64, _I64, _I32, _P, _SZ, _P]),
     "nnue_ft_backward_noalloc": (_I32, [_P, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I32, _P]),
     "nnue_ft_noalloc_scratch_bytes": (_SZ, []),
     "nnue_ft_backward_prepare": (_I32, [_P, _P, _I64, _I32, _I32, _I64, _I32, _P, _SZ, _P]),

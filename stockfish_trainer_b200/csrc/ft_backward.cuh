@@ -393,6 +393,8 @@ struct SegParams {
   int32_t heavy_cap;
   int32_t chunk0;             // first column chunk of this launch (blockIdx.y offset)
   int32_t n_stream_warps;
+  int32_t row_begin;          // rows [row_begin, row_end) of dW are produced by this call
+  int32_t row_end;
   Geom g;
 };
 
@@ -472,8 +474,8 @@ __global__ void __launch_bounds__(kBlock) ft_segsum_walk_kernel(const SegParams 
   const int c0 = p.g.begin(chunk);
   const int width = p.g.width(chunk);
   const int64_t row_vec = p.g.n_vec;
-  const int64_t f = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (f >= p.T) return;
+  const int64_t f = p.row_begin + (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  if (f >= p.row_end) return;
   if (p.row_kind[f]) return;
   bool ok[V];
 #pragma unroll
@@ -547,6 +549,7 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
   const int nh = *p.n_heavy < p.heavy_cap ? *p.n_heavy : p.heavy_cap;
   if (slot >= nh) return;
   const int64_t f = p.heavy_list[slot];
+  if (f < p.row_begin || f >= p.row_end) return;
   const int col = c0 + piece * 32 + lane;
   const bool ok1 = piece * 32 + lane < width;
   const int64_t row_vec = p.g.n_vec;

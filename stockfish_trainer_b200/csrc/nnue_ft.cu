@@ -363,7 +363,7 @@ template <typename VT, int V, int U>
 void launch_segsum_vu(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
   count_launch();
-  dim3 grid((unsigned)ceil_div(p.T, kWarpsPerBlock), (unsigned)n_chunks);
+  dim3 grid((unsigned)ceil_div(p.row_end - p.row_begin, kWarpsPerBlock), (unsigned)n_chunks);
   ft_segsum_walk_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
 }
 
@@ -494,9 +494,13 @@ int launch_segsum_stream(const SegParams& p, cudaStream_t s) {
 }
 
 int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w, float* dW, float* dB,
-               int32_t accumulate, cudaStream_t s) {
+               int32_t accumulate, int64_t row_begin, int64_t row_end, bool with_bias, cudaStream_t s) {
+  if (row_begin < 0 || row_end > pl.T || row_begin > row_end)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "backward_apply: row range [%lld, %lld) outside [0, %lld)",
+                (long long)row_begin, (long long)row_end, (long long)pl.T);
+  if (row_begin == row_end && !with_bias) return NNUE_OK;
   const bool v4 = (pl.C % 4 == 0) && aligned16(g0) && (pl.P == 1 || aligned16(g1)) && aligned16(dW) &&
-                  aligned16(dB) && aligned16(w.partial);
+                  (!with_bias || aligned16(dB)) && aligned16(w.partial);
   SegParams p{};
   p.dout[0] = g0;
   p.dout[1] = pl.P == 2 ? g1 : g0;
@@ -513,11 +517,15 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   p.heavy_cap = (int32_t)pl.heavy_cap;
   p.first_row = w.first_row;
   p.n_stream_warps = (int32_t)pl.n_stream_warps;
+  p.row_begin = (int32_t)row_begin;
+  p.row_end = (int32_t)row_end;
   p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec, g_tune.bwd_exact_chunks)
              : make_geom(pl.C, g_tune.bwd_chunk_vec * 4, g_tune.bwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "backward: column chunk too wide");
 
-  const bool stream = v4 && g_tune.bwd_variant == 0 && lanes_per_row(p.g) <= 2;
+  const bool full_range = row_begin == 0 && row_end == pl.T;
+  const bool stream = v4 && g_tune.bwd_variant == 0 && lanes_per_row(p.g) <= 2 && full_range;
+  const bool rows = row_end > row_begin;
   DeviceAux* aux = nullptr;
   int rc = device_aux(&aux);
   if (rc != NNUE_OK) return rc;
@@ -526,19 +534,19 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     std::lock_guard<std::mutex> lock(g_aux_mu);
     if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
       return check_launch("backward_apply: fork");
-    if (!stream) {
+    if (!stream && rows) {
       rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
       if (rc != NNUE_OK) return rc;
     }
-    launch_colsum(g0, g1, pl, v4, w.partial, dB, p.accumulate, aux->side);
+    if (with_bias) launch_colsum(g0, g1, pl, v4, w.partial, dB, p.accumulate, aux->side);
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
   }
   if (stream) {
     rc = lanes_per_row(p.g) == 1 ? launch_segsum_stream<1>(p, s) : launch_segsum_stream<2>(p, s);
     if (rc != NNUE_OK) return rc;
-  } else if (v4) {
+  } else if (rows && v4) {
     launch_segsum_light<float4>(p, s);
-  } else {
+  } else if (rows) {
     launch_segsum_light<float>(p, s);
   }
   // A later record of `join` by another call is further down the same
@@ -720,8 +728,24 @@ int nnue_ft_backward_apply(const float* grad0, const float* grad1, int64_t batch
   if (!workspace || workspace_bytes < pl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(NNUE_ERR_WORKSPACE, "backward_apply: workspace missing, misaligned or smaller than %zu bytes",
                 pl.total);
-  return apply_impl(grad0, grad1, pl, carve(pl, workspace), weight_grad, bias_grad, accumulate,
+  return apply_impl(grad0, grad1, pl, carve(pl, workspace), weight_grad, bias_grad, accumulate, 0, pl.T, true,
                     static_cast<cudaStream_t>(stream));
+}
+
+int nnue_ft_backward_apply_rows(const float* grad0, const float* grad1, int64_t batch, int32_t max_active,
+                                int32_t n_persp, int64_t num_inputs, int32_t output_size, float* weight_grad,
+                                float* bias_grad, int32_t accumulate, int64_t row_begin, int64_t row_end,
+                                int32_t with_bias, void* workspace, size_t workspace_bytes, void* stream) {
+  BwdPlan pl;
+  int rc = make_plan(batch, max_active, num_inputs, output_size, n_persp, pl);
+  if (rc != NNUE_OK) return rc;
+  if (!weight_grad || (with_bias && !bias_grad) || (batch > 0 && (!grad0 || (n_persp == 2 && !grad1))))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "backward_apply_rows: null pointer");
+  if (!workspace || workspace_bytes < pl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(NNUE_ERR_WORKSPACE, "backward_apply_rows: workspace missing, misaligned or smaller than %zu bytes",
+                pl.total);
+  return apply_impl(grad0, grad1, pl, carve(pl, workspace), weight_grad, bias_grad, accumulate, row_begin, row_end,
+                    with_bias != 0, static_cast<cudaStream_t>(stream));
 }
 
 int nnue_ft_backward(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active, const float* grad0,

@@ -15,6 +15,7 @@ from __future__ import annotations
 import datetime
 import os
 from dataclasses import dataclass
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -79,3 +80,56 @@ class GradientBuffer:
             for part in torch.tensor_split(self.flat, chunks):
                 dist.all_reduce(part, group=group)
         self.flat.div_(world_size)
+
+
+_comm_streams: dict[int, torch.cuda.Stream] = {}
+
+
+def _comm_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _comm_streams:
+        _comm_streams[idx] = torch.cuda.Stream(device=idx)
+    return _comm_streams[idx]
+
+
+def backward_allreduce_overlapped(grad0, grad1, batch: int, max_active: int, buf: GradientBuffer,
+                                  workspace: torch.Tensor, world_size: int, n_blocks: int = 4,
+                                  group=None, comm_stream: Optional[torch.cuda.Stream] = None) -> None:
+    """Dense FT gradients of this rank's shard, averaged over all ranks, with
+    the exchange overlapped with the computation.
+
+    The weight gradient is produced in ``n_blocks`` row blocks
+    (nnue_ft_backward_apply_rows); as soon as a block is written, its rows are
+    allreduced on a separate stream while the next block is computed, so only
+    the last block's exchange is exposed.  The bias gradient travels with the
+    last block (it sits after the weight in the flat buffer).  Requires
+    ``backward_prepare`` (or ``forward_pair_prepare``) to have filled
+    ``workspace`` on the current stream."""
+    from .feature_transformer import ops
+
+    T, C = buf.weight.shape
+    if world_size <= 1:
+        ops.backward_apply(grad0, grad1, batch, max_active, buf.weight, buf.bias, False, workspace)
+        return
+    compute = torch.cuda.current_stream(buf.flat.device)
+    comm = comm_stream or _comm_stream(buf.flat.device)
+    n_blocks = max(1, min(n_blocks, T))
+    bounds = [T * i // n_blocks for i in range(n_blocks + 1)]
+    avg = dist.get_backend(group) == "nccl"
+    works = []
+    for i in range(n_blocks):
+        last = i == n_blocks - 1
+        ops.backward_apply_rows(grad0, grad1, batch, max_active, buf.weight, buf.bias, False, workspace,
+                                bounds[i], bounds[i + 1], with_bias=last)
+        ready = torch.cuda.Event()
+        ready.record(compute)
+        part = buf.flat[bounds[i] * C:] if last else buf.flat[bounds[i] * C: bounds[i + 1] * C]
+        with torch.cuda.stream(comm):
+            comm.wait_event(ready)
+            op = dist.ReduceOp.AVG if avg else dist.ReduceOp.SUM
+            works.append(dist.all_reduce(part, op=op, group=group, async_op=True))
+    for w in works:
+        w.wait()  # the current stream waits for the collective
+    if not avg:
+        buf.flat.div_(world_size)
+

@@ -139,6 +139,26 @@ def backward_apply(grad0, grad1, batch: int, max_active: int, weight_grad, bias_
                      workspace.data_ptr(), workspace.numel(), _stream_ptr(dev))
 
 
+def backward_apply_rows(grad0, grad1, batch: int, max_active: int, weight_grad, bias_grad, accumulate: bool,
+                        workspace: torch.Tensor, row_begin: int, row_end: int, with_bias: bool) -> None:
+    """backward_apply for weight-gradient rows [row_begin, row_end) only; the
+    bias gradient is produced when ``with_bias``."""
+    dev = weight_grad.device
+    _check(weight_grad, "weight_grad", torch.float32, 2, dev)
+    _check(grad0, "grad_output_0", torch.float32, 2, dev)
+    if with_bias:
+        _check(bias_grad, "bias_grad", torch.float32, 1, dev)
+    P = 1 if grad1 is None else 2
+    if P == 2:
+        _check(grad1, "grad_output_1", torch.float32, 2, dev)
+    T, C = weight_grad.shape
+    with torch.cuda.device(dev):
+        _native.call("nnue_ft_backward_apply_rows", grad0.data_ptr(), 0 if grad1 is None else grad1.data_ptr(),
+                     batch, max_active, P, T, C, weight_grad.data_ptr(), bias_grad.data_ptr() if with_bias else 0,
+                     int(bool(accumulate)), row_begin, row_end, int(bool(with_bias)), workspace.data_ptr(),
+                     workspace.numel(), _stream_ptr(dev))
+
+
 def backward_into(idx0, idx1, grad0, grad1, weight_grad, bias_grad, accumulate: bool,
                   workspace: torch.Tensor | None = None) -> None:
     """Full backward for one (idx1 is None) or two perspectives."""

@@ -54,6 +54,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["headline", "halfka", "quantized"], default="headline",
+                   help="headline: BASELINE configs[2]/[3] (the driver's metric); halfka: configs[1] "
+                        "(HalfKAv2_hm^, B=16384, phases reported separately); quantized: configs[4] "
+                        "(int16 forward, HalfKAv2_hm^, B=65536)")
     p.add_argument("--batch", type=int, default=65536, help="global batch (positions)")
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--feature-set", default=FEATURE_SET)
@@ -444,8 +448,10 @@ def run_ours(args):
         cpu = cpu_baseline(white, black, W.cpu().numpy(), args.seed, args.cpu_seconds)
 
     if rank == 0:
+        metric = METRIC if args.workload == "headline" else \
+            f"positions/s {args.feature_set} FT fwd+bwd @B={args.batch} L1={L1}"
         line = {
-            "metric": METRIC,
+            "metric": metric,
             "value": value,
             "unit": "positions/s",
             "n_gpus": world,
@@ -474,6 +480,58 @@ def run_ours(args):
     return 0
 
 
+def run_quantized(args):
+    """int16 quantised FT forward of both perspectives,
+    HalfKAv2_hm^ export tables (22528 x 1040 int16 + 8 int32 PSQT) produced
+    from random fp32 weights by the serializer's quantisation."""
+    import torch
+
+    from stockfish_trainer_b200 import _native, positions
+    from stockfish_trainer_b200.feature_transformer import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    fs = "HalfKAv2_hm^"
+    B = args.batch
+    white, black, _ = positions.synthetic_batch(B, fs, seed=args.seed)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    W = torch.randn(24576, C, device=dev, generator=gen) * 0.01
+    V = torch.randn(768, C, device=dev, generator=gen) * 0.002
+    wq, pq = ops.halfka_export_quantize(W, V, L1)
+    bq = ops.quantize_i16((torch.randn(L1, device=dev, generator=gen) * 0.05).contiguous(), 255.0)
+    i0, i1 = torch.from_numpy(white).to(dev), torch.from_numpy(black).to(dev)
+    step = lambda: ops.quantized_forward_pair(i0, i1, wq, pq, bq, True)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    nnz = int((white >= 0).sum() + (black >= 0).sum())
+    row_bytes = L1 * 2 + NPSQT * 4
+    a_bytes = nnz * row_bytes + 2 * B * row_bytes + 2 * B * white.shape[1] * 4
+    peak, src = hbm_peak()
+    emit({
+        "metric": "positions/s int16 FT forward (both perspectives) @B=65536 L1=1040, HalfKAv2_hm^",
+        "value": B / (ms / 1e3), "unit": "positions/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "i16", "data": DATA,
+        "config": {"workload": "int16 quantised FT forward, HalfKAv2_hm^ export tables, training indices mapped "
+                               "in-kernel", "batch": B, "L1": L1, "psqt": NPSQT, "table_rows": 22528},
+        "roofline": {"bound": "hbm", "achieved": a_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": a_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
+                     "kernel": "ft_qforward_kernel", "algorithmic_bytes": a_bytes,
+                     "peak_source": f"{src} hbm_gbs"},
+        "gpu_launches": int(_native.launch_count() - l0),
+    })
+    return 0
+
+
 _JSON_FD = None
 
 
@@ -497,6 +555,12 @@ def main():
     os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "quantized":
+        return run_quantized(args)
+    if args.workload == "halfka":
+        args.feature_set = "HalfKAv2_hm^"
+        if args.batch == 65536:
+            args.batch = 16384
     return run_ours(args)
 
 

@@ -353,9 +353,11 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
   classify_rows_kernel<<<(unsigned)ceil_div(pl.T, kBlock), kBlock, 0, s>>>(
       w.seg, (int32_t)pl.T, pl.P, (int32_t)std::min<int64_t>(pl.heavy_threshold, INT32_MAX),
       (int32_t)pl.heavy_cap, w.nheavy, w.heavy, w.kind);
-  count_launch();
-  warp_ranges_kernel<<<(unsigned)ceil_div(pl.T + 1, kBlock), kBlock, 0, s>>>(
-      w.seg, (int32_t)pl.T, pl.P, (int32_t)pl.epw, (int32_t)pl.n_stream_warps, w.first_row);
+  if (g_tune.bwd_variant == 0) {  // only the streaming apply uses the per-warp row ranges
+    count_launch();
+    warp_ranges_kernel<<<(unsigned)ceil_div(pl.T + 1, kBlock), kBlock, 0, s>>>(
+        w.seg, (int32_t)pl.T, pl.P, (int32_t)pl.epw, (int32_t)pl.n_stream_warps, w.first_row);
+  }
   return check_launch("backward_prepare");
 }
 

@@ -54,10 +54,11 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["headline", "halfka", "quantized"], default="headline",
+    p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe"], default="headline",
                    help="headline: BASELINE configs[2]/[3] (the driver's metric); halfka: configs[1] "
                         "(HalfKAv2_hm^, B=16384, phases reported separately); quantized: configs[4] "
-                        "(int16 forward, HalfKAv2_hm^, B=65536)")
+                        "(int16 forward, HalfKAv2_hm^, B=65536); gather-probe: random-row gather bandwidth "
+                        "versus table size (the ceiling for the FT gathers)")
     p.add_argument("--batch", type=int, default=65536, help="global batch (positions)")
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--feature-set", default=FEATURE_SET)
@@ -480,6 +481,40 @@ def run_ours(args):
     return 0
 
 
+def run_gather_probe(args):
+    """Random 512-byte-row gather bandwidth versus table size."""
+    import torch
+
+    from stockfish_trainer_b200 import _native
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_warps, per_warp = 148 * 32, 2048
+    table = torch.zeros((512 << 20) // 4, device=dev)
+    out = torch.empty(n_warps * 128, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    curve = {}
+    for mb in (16, 32, 48, 64, 80, 96, 128, 192, 256, 512):
+        rows = (mb << 20) // 512
+        idx = torch.randint(0, rows, (n_warps * per_warp,), dtype=torch.int32, device=dev)
+        run = lambda: _native.call("nnue_ft_gather_probe", table.data_ptr(), rows, idx.data_ptr(), per_warp, n_warps,
+                                   out.data_ptr(), stream)
+        for _ in range(3):
+            run()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(max(args.steps, 5)):
+            run()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / max(args.steps, 5)
+        curve[f"{mb}MB"] = round(n_warps * per_warp * 512 / (ms / 1e3) / 1e9, 1)
+    emit({"metric": "GB/s random 512-byte-row gather vs table size", "unit": "GB/s", "value": max(curve.values()),
+          "curve": curve, "warps": n_warps, "rows_in_flight_per_warp": 8, "higher_is_better": True,
+          "hbm_peak": hbm_peak()[0]})
+    return 0
+
+
 def run_quantized(args):
     """int16 quantised FT forward of both perspectives,
     HalfKAv2_hm^ export tables (22528 x 1040 int16 + 8 int32 PSQT) produced
@@ -557,6 +592,8 @@ def main():
         return run_reference(args)
     if args.workload == "quantized":
         return run_quantized(args)
+    if args.workload == "gather-probe":
+        return run_gather_probe(args)
     if args.workload == "halfka":
         args.feature_set = "HalfKAv2_hm^"
         if args.batch == 65536:

@@ -197,6 +197,14 @@ int nnue_ft_quantize_i16(const float *x, int64_t n, float scale, int16_t *q, voi
  * asserts 60720, feature_extraction.rs:826). */
 int nnue_threat_table_total(void);
 
+/* Measurement only (no counterpart in the reference): n_warps warps each sum
+ * per_warp random 512-byte rows (32 float4) of `table` ([rows, 128] fp32),
+ * 8 row loads in flight per warp, indices idx [n_warps * per_warp] in
+ * [0, rows).  The achieved bandwidth versus table size is the ceiling for
+ * the FT's gathers.  per_warp % 32 == 0, n_warps % 8 == 0; out: [n_warps, 128]. */
+int nnue_ft_gather_probe(const float *table, int64_t rows, const int32_t *idx, int32_t per_warp, int32_t n_warps,
+                         float *out, void *stream);
+
 /* ---- host-side synthetic inputs (no GPU needed) --------------------------
  * Seeded random positions: per position an independent splitmix64 stream;
  * kings on distinct uniform squares; U{0..30} other pieces of uniform type

@@ -568,6 +568,33 @@ int check_bwd_args(const int32_t* idx0, const int32_t* idx1, int P, void* ws, si
 }
 
 // ---------------------------------------------------------------------------
+// Gather probe (measurement only): every warp sums `per_warp` random 512-byte
+// rows of a table, 8 row loads in flight per warp -- the FT's access pattern
+// with none of its bookkeeping.  Its bandwidth versus table size is the
+// ceiling a gather kernel can reach from L2 / HBM on this GPU.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kBlock) gather_probe_kernel(const float4* __restrict__ table, int64_t rows,
+                                                              const int32_t* __restrict__ idx, int32_t per_warp,
+                                                              float4* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int32_t* my = idx + wid * per_warp;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j0 = 0; j0 + 32 <= per_warp; j0 += 32) {
+    int r = __ldg(my + j0 + lane);
+    r = (unsigned)r < (unsigned)rows ? r : 0;
+    for (int u0 = 0; u0 < 32; u0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(table + (int64_t)__shfl_sync(kFull, r, u0 + u) * 32 + lane);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) Vec<float4>::add(acc, v[u]);
+    }
+  }
+  out[wid * 32 + lane] = acc;
+}
+
+// ---------------------------------------------------------------------------
 // quantised forward
 // ---------------------------------------------------------------------------
 template <int VQ>
@@ -855,6 +882,17 @@ int nnue_ft_backward_noalloc(const int32_t* idx0, const int32_t* idx1, int64_t b
   if (rc != NNUE_OK) return rc;
   return nnue_ft_backward(idx0, idx1, batch, max_active, grad0, grad1, n_persp, num_inputs, output_size, weight_grad,
                           bias_grad, accumulate, scratch, kNoAllocScratchBytes, stream);
+}
+
+int nnue_ft_gather_probe(const float* table, int64_t rows, const int32_t* idx, int32_t per_warp, int32_t n_warps,
+                         float* out, void* stream) {
+  if (!table || !idx || !out || rows <= 0 || per_warp < 32 || per_warp % 32 != 0 || n_warps <= 0 ||
+      n_warps % kWarpsPerBlock != 0 || !aligned16(table) || !aligned16(out))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "gather_probe: bad arguments");
+  count_launch();
+  gather_probe_kernel<<<(unsigned)(n_warps / kWarpsPerBlock), kBlock, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float4*>(table), rows, idx, per_warp, reinterpret_cast<float4*>(out));
+  return check_launch("gather_probe");
 }
 
 }  // extern "C"

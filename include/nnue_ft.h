@@ -61,8 +61,11 @@ const char *nnue_ft_last_error(void);
 int nnue_ft_device_errors(uint32_t *flags, int clear);
 
 /* Tuning knobs (names: "fwd_chunk_vec", "fwd_items_per_warp", "fwd_unroll",
- * "bwd_chunk_vec", "bwd_unroll", "heavy_threshold", "heavy_cap",
- * "sort_tile_rows", "sort_tile", "colsum_parts").
+ * "fwd_min_blocks", "fwd_exact_chunks", "bwd_chunk_vec", "bwd_unroll",
+ * "bwd_min_blocks", "bwd_exact_chunks", "bwd_variant", "bwd_stream_cfg",
+ * "bwd_entries_per_warp", "heavy_threshold", "heavy_cap", "sort_tile_rows",
+ * "sort_tile", "colsum_parts"); unknown names and out-of-range values are
+ * rejected with NNUE_ERR_INVALID_ARGUMENT.
  * Process-wide; change them only while no call is in flight and never between
  * a backward_prepare and its backward_apply. */
 int nnue_ft_set_param(const char *name, int64_t value);

@@ -409,15 +409,38 @@ __device__ __forceinline__ int decode_position(int v, int q, int64_t B) {
   return (int)b;
 }
 
-// acc[v] += dOut_q[b, cols] for every entry of sorted_b[s, e) (perspective q), ascending.
+template <typename VT, int V>
+__device__ __forceinline__ void seg_write(const SegParams& p, int64_t f, int col, const VT (&tot)[V],
+                                          const bool (&ok)[V], bool touched) {
+  using Ops = Vec<VT>;
+  VT* dst = reinterpret_cast<VT*>(p.dW) + f * (int64_t)p.g.n_vec + col;
+  if (p.accumulate) {
+    if (!touched) return;
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+      if (ok[v]) {
+        VT cur = dst[32 * v];
+        Ops::add(cur, tot[v]);
+        dst[32 * v] = cur;
+      }
+  } else {
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+      if (ok[v]) dst[32 * v] = tot[v];
+  }
+}
+
+// acc[v] += dOut_q[b, cols] for the entries of sorted_b[s, e) (perspective q),
+// ascending, where `my` already holds the decoded first 32 positions
+// (lane i: entry s + i).  Later groups of 32 are loaded as needed.
 template <typename VT, int V, int U>
 __device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src, int64_t row_vec,
-                                        const int32_t* __restrict__ sb, int s, int e, int q, int64_t B,
-                                        const bool (&ok)[V], int lane) {
+                                                  const int32_t* __restrict__ sb, int s, int e, int q, int64_t B,
+                                                  int my, const bool (&ok)[V], int lane) {
   using Ops = Vec<VT>;
   for (int j0 = s; j0 < e; j0 += 32) {
     const int cnt = e - j0 < 32 ? e - j0 : 32;
-    const int my = lane < cnt ? decode_position(__ldg(sb + j0 + lane), q, B) : -1;
+    if (j0 != s) my = lane < cnt ? decode_position(__ldg(sb + j0 + lane), q, B) : -1;
     for (int u0 = 0; u0 < cnt; u0 += U) {
       int rows[U];
       bool has[U];
@@ -441,33 +464,17 @@ __device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src
   }
 }
 
-template <typename VT, int V>
-__device__ __forceinline__ void seg_write(const SegParams& p, int64_t f, int col, const VT (&tot)[V],
-                                          const bool (&ok)[V], bool touched) {
-  using Ops = Vec<VT>;
-  VT* dst = reinterpret_cast<VT*>(p.dW) + f * (int64_t)p.g.n_vec + col;
-  if (p.accumulate) {
-    if (!touched) return;
-#pragma unroll
-    for (int v = 0; v < V; ++v)
-      if (ok[v]) {
-        VT cur = dst[32 * v];
-        Ops::add(cur, tot[v]);
-        dst[32 * v] = cur;
-      }
-  } else {
-#pragma unroll
-    for (int v = 0; v < V; ++v)
-      if (ok[v]) dst[32 * v] = tot[v];
-  }
-}
-
-// Fallback light rows (any geometry / the scalar path): one warp per (row,
-// column chunk); per perspective the row's entries are read 32 at a time and
-// broadcast with __shfl_sync, U dOut rows in flight per batch.  Heavy rows
-// are left to ft_segsum_heavy_kernel.
-template <typename VT, int V, int U>
-__global__ void __launch_bounds__(kBlock) ft_segsum_walk_kernel(const SegParams p) {
+// Light rows: one warp per (row, column chunk), U dOut rows in flight per
+// batch, positions broadcast from registers with __shfl_sync.  The row's
+// segment bounds (both perspectives) and its heavy flag arrive in ONE round
+// trip and the first 32 positions of both perspectives in a second, so a
+// row costs two dependent round trips before its data batches start.  The
+// kernel is latency-bound: the bytes in flight per SM are resident warps x U
+// x one 512-byte row slice, so MINB (resident blocks the register budget is
+// sized for) matters as much as U.  Heavy rows are left to
+// ft_segsum_heavy_kernel.
+template <typename VT, int V, int U, int MINB = 1>
+__global__ void __launch_bounds__(kBlock, MINB) ft_segsum_light_kernel(const SegParams p) {
   using Ops = Vec<VT>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunk = p.chunk0 + blockIdx.y;
@@ -476,28 +483,33 @@ __global__ void __launch_bounds__(kBlock) ft_segsum_walk_kernel(const SegParams 
   const int64_t row_vec = p.g.n_vec;
   const int64_t f = p.row_begin + (int64_t)blockIdx.x * kWarpsPerBlock + warp;
   if (f >= p.row_end) return;
-  if (p.row_kind[f]) return;
+  const int P = p.P;
+  const int bnd = lane <= P ? p.seg_start[f * P + lane] : 0;
+  const int kind = p.row_kind[f];
+  const int s0 = __shfl_sync(kFull, bnd, 0);
+  const int s1 = __shfl_sync(kFull, bnd, 1);
+  const int e1 = __shfl_sync(kFull, bnd, P);
+  if (kind) return;
+  const int g0 = s0 + lane < s1 ? decode_position(__ldg(p.sorted_b + s0 + lane), 0, p.B) : -1;
+  const int g1 = (P == 2 && s1 + lane < e1) ? decode_position(__ldg(p.sorted_b + s1 + lane), 1, p.B) : -1;
   bool ok[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) ok[v] = lane + 32 * v < width;
   VT tot[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) tot[v] = Ops::zero();
-  for (int q = 0; q < p.P; ++q) {
-    VT acc[V];
+  seg_sum<VT, V, U>(tot, reinterpret_cast<const VT*>(p.dout[0]) + c0 + lane, row_vec, p.sorted_b, s0, s1,
+                              0, p.B, g0, ok, lane);
+  if (P == 2) {
+    VT acc1[V];
 #pragma unroll
-    for (int v = 0; v < V; ++v) acc[v] = Ops::zero();
-    const int s = p.seg_start[f * p.P + q], e = p.seg_start[f * p.P + q + 1];
-    const VT* src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]) + c0 + lane;
-    seg_sum<VT, V, U>(acc, src, row_vec, p.sorted_b, s, e, q, p.B, ok, lane);
+    for (int v = 0; v < V; ++v) acc1[v] = Ops::zero();
+    seg_sum<VT, V, U>(acc1, reinterpret_cast<const VT*>(p.dout[1]) + c0 + lane, row_vec, p.sorted_b, s1,
+                                e1, 1, p.B, g1, ok, lane);
 #pragma unroll
-    for (int v = 0; v < V; ++v) {
-      if (q == 0) tot[v] = acc[v];
-      else Ops::add(tot[v], acc[v]);
-    }
+    for (int v = 0; v < V; ++v) Ops::add(tot[v], acc1[v]);
   }
-  const bool touched = p.seg_start[(f + 1) * p.P] > p.seg_start[f * p.P];
-  seg_write<VT, V>(p, f, c0 + lane, tot, ok, touched);
+  seg_write<VT, V>(p, f, c0 + lane, tot, ok, e1 > s0);
 }
 
 // ---------------------------------------------------------------------------

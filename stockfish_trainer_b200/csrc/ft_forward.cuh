@@ -63,8 +63,8 @@ __device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, 
   return n;
 }
 
-template <typename VT, int V, int U>
-__global__ void __launch_bounds__(kBlock) ft_forward_kernel(const FwdParams p) {
+template <typename VT, int V, int U, int MINB = 1>
+__global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParams p) {
   using Ops = Vec<VT>;
   __shared__ int s_list[kWarpsPerBlock][32 * kIdxGroups];
   const int lane = threadIdx.x & 31;

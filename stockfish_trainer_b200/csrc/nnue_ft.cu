@@ -49,11 +49,13 @@ struct Tuning {
   int64_t fwd_chunk_vec = 53;       // forward column chunk, in 16-byte vectors
   int64_t fwd_items_per_warp = 16;  // (perspective, position) items per warp
   int64_t fwd_unroll = 4;          // table rows in flight per warp (4 or 8)
-  int64_t bwd_unroll = 4;          // dOut rows in flight per warp, light rows (4 or 8)
+  int64_t bwd_unroll = 4;          // dOut rows per batch, light rows (2, 4 or 8)
   int64_t bwd_entries_per_warp = 2048;  // streaming backward: sorted entries per warp
+  int64_t fwd_min_blocks = 2;      // forward: registers sized for 2, 3 or 4 resident blocks (else compiler's choice)
+  int64_t bwd_min_blocks = 6;      // light rows: registers sized for 4, 5, 6 or 8 resident blocks (else compiler's)
   int64_t fwd_exact_chunks = 0;    // 1: full-width chunks + narrow tail; 0: balanced widths
   int64_t bwd_exact_chunks = 1;
-  int64_t bwd_variant = 1;         // 1: per-row walk + heavy-row kernel, 0: streaming cp.async segment sums
+  int64_t bwd_variant = 1;  // 1: warp per light row (+ heavy-row kernel); 0: streaming
   int64_t bwd_stream_cfg = 0;      // streaming kernel shape (stages / group / warps per block)
   int64_t bwd_chunk_vec = 32;      // backward column chunk, in 16-byte vectors
   int64_t heavy_threshold = 256;   // rows with more entries are split finer
@@ -75,11 +77,13 @@ ParamRef* params() {
       {"fwd_chunk_vec", &g_tune.fwd_chunk_vec, 0, 1 << 20},
       {"fwd_items_per_warp", &g_tune.fwd_items_per_warp, 1, 1024},
       {"fwd_unroll", &g_tune.fwd_unroll, 4, 8},
-      {"bwd_unroll", &g_tune.bwd_unroll, 4, 8},
+      {"bwd_unroll", &g_tune.bwd_unroll, 2, 8},
       {"bwd_entries_per_warp", &g_tune.bwd_entries_per_warp, 32, 1 << 24},
       {"fwd_exact_chunks", &g_tune.fwd_exact_chunks, 0, 1},
       {"bwd_exact_chunks", &g_tune.bwd_exact_chunks, 0, 1},
       {"bwd_variant", &g_tune.bwd_variant, 0, 1},
+      {"fwd_min_blocks", &g_tune.fwd_min_blocks, 0, 4},
+      {"bwd_min_blocks", &g_tune.bwd_min_blocks, 0, 8},
       {"bwd_stream_cfg", &g_tune.bwd_stream_cfg, 0, 5},
       {"bwd_chunk_vec", &g_tune.bwd_chunk_vec, 0, 1 << 20},
       {"heavy_threshold", &g_tune.heavy_threshold, 1, int64_t(1) << 40},
@@ -125,6 +129,14 @@ void launch_forward_vu(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(warps, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
+  if constexpr (V <= 2) {
+    switch (g_tune.fwd_min_blocks) {
+      case 2: ft_forward_kernel<VT, V, U, 2><<<grid, kBlock, 0, s>>>(p); return;
+      case 3: ft_forward_kernel<VT, V, U, 3><<<grid, kBlock, 0, s>>>(p); return;
+      case 4: ft_forward_kernel<VT, V, U, 4><<<grid, kBlock, 0, s>>>(p); return;
+      default: break;
+    }
+  }
   ft_forward_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
 }
 
@@ -364,15 +376,25 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
 template <typename VT, int V, int U>
 void launch_segsum_vu(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
-  count_launch();
   dim3 grid((unsigned)ceil_div(p.row_end - p.row_begin, kWarpsPerBlock), (unsigned)n_chunks);
-  ft_segsum_walk_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
+  count_launch();
+  if constexpr (V <= 2) {
+    switch (g_tune.bwd_min_blocks) {
+      case 4: ft_segsum_light_kernel<VT, V, U, 4><<<grid, kBlock, 0, s>>>(p); return;
+      case 5: ft_segsum_light_kernel<VT, V, U, 5><<<grid, kBlock, 0, s>>>(p); return;
+      case 6: ft_segsum_light_kernel<VT, V, U, 6><<<grid, kBlock, 0, s>>>(p); return;
+      case 8: ft_segsum_light_kernel<VT, V, U, 8><<<grid, kBlock, 0, s>>>(p); return;
+      default: break;
+    }
+  }
+  ft_segsum_light_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
 }
 
 template <typename VT, int V>
 void launch_segsum_v(const SegParams& p, int chunk0, int n_chunks, cudaStream_t s) {
   if constexpr (V <= 2) {
     if (g_tune.bwd_unroll >= 8) launch_segsum_vu<VT, V, 8>(p, chunk0, n_chunks, s);
+    else if (g_tune.bwd_unroll <= 2) launch_segsum_vu<VT, V, 2>(p, chunk0, n_chunks, s);
     else launch_segsum_vu<VT, V, 4>(p, chunk0, n_chunks, s);
   } else if constexpr (V <= 4) {
     launch_segsum_vu<VT, V, 4>(p, chunk0, n_chunks, s);

@@ -512,35 +512,6 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_segsum_light_kernel(const Seg
   seg_write<VT, V>(p, f, c0 + lane, tot, ok, e1 > s0);
 }
 
-// ---------------------------------------------------------------------------
-// cp.async helpers: every lane copies its own 16 (or 4) bytes into a lane-
-// private shared-memory slot and later reads back only what it copied, so
-// no barrier is needed; the group count bounds what is still in flight.
-// ---------------------------------------------------------------------------
-template <typename VT>
-__device__ __forceinline__ void cp_async_vec(VT* smem_dst, const VT* gsrc, bool pred);
-
-template <>
-__device__ __forceinline__ void cp_async_vec<float4>(float4* smem_dst, const float4* gsrc, bool pred) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
-  const int n = pred ? 16 : 0;  // 0 source bytes: zero-fill, source not read
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gsrc), "r"(n) : "memory");
-}
-
-template <>
-__device__ __forceinline__ void cp_async_vec<float>(float* smem_dst, const float* gsrc, bool pred) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
-  const int n = pred ? 4 : 0;
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(gsrc), "r"(n) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
 // Heavy rows of the fallback path: one warp per 32-vector piece of a column
 // chunk streams the row's dOut slices through a kHeavyStages-deep ring.
 constexpr int kHeavyWarps = 2;

@@ -8,11 +8,10 @@
 // Mapping: one warp per (perspective, position) item and column chunk, a few
 // consecutive items per warp.  The warp reads all index slots of an item at
 // once (8 coalesced loads of 32), compacts the valid ones into a per-warp
-// shared-memory list (ascending k) and walks it U rows at a time: all U x V
-// 128-bit row loads are issued before the U x V adds.  The next item's
-// indices are loaded while the current item's rows are in flight, so the
-// index latency is hidden.  Lanes own fixed column vectors, which keeps the
-// per-column add order.
+// shared-memory list (ascending k) and streams the rows through a register
+// queue (below).  The next item's indices are loaded while the current
+// item's rows are in flight, so the index latency is hidden.  Lanes own fixed
+// column vectors, which keeps the per-column add order.
 #pragma once
 
 #include "common.cuh"
@@ -46,9 +45,9 @@ __device__ __forceinline__ void load_index_groups(const int32_t* __restrict__ ir
   }
 }
 
-// Writes the valid indices of f[] (ascending slot order) to `list`; returns
-// how many.  Indices outside [-1, T) are flagged and dropped.
-__device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, int* list, int lane) {
+// Writes the valid indices of f[] (ascending slot order), times `scale`, to
+// `list`; returns how many.  Indices outside [-1, T) are flagged and dropped.
+__device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, int* list, int lane, int scale = 1) {
   const unsigned lt = lanemask_lt();
   int n = 0;
 #pragma unroll
@@ -56,14 +55,21 @@ __device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, 
     const bool valid = (unsigned)f[g] < (unsigned)T;
     if (!valid && f[g] != -1) flag_error(kErrBadIndex);
     const unsigned m = __ballot_sync(kFull, valid);
-    if (valid) list[n + __popc(m & lt)] = f[g];
+    if (valid) list[n + __popc(m & lt)] = f[g] * scale;
     n += __popc(m);
   }
   __syncwarp();
   return n;
 }
 
-template <typename VT, int V, int U, int MINB = 1>
+// The rows of an item stream through a D-slot register queue: consuming
+// slot d immediately re-issues it with the row D further on, so D rows stay
+// in flight for the whole item.  The compacted list holds row OFFSETS (index
+// x row vectors, int32) and the bias is re-read from L1 per item.  The
+// kernel is latency-bound: bytes in flight per SM are resident warps x D x
+// one row slice, so MINB (resident blocks the register budget is sized for)
+// matters as much as D.
+template <typename VT, int V, int D, int MINB = 1>
 __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParams p) {
   using Ops = Vec<VT>;
   __shared__ int s_list[kWarpsPerBlock][32 * kIdxGroups];
@@ -72,30 +78,22 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
   const int chunk = p.chunk0 + blockIdx.y;
   const int c0 = p.g.begin(chunk);
   const int width = p.g.width(chunk);
-
   bool ok[V];
-  VT bias_r[V];
-  const VT* __restrict__ bvec = reinterpret_cast<const VT*>(p.bias) + c0 + lane;
 #pragma unroll
-  for (int v = 0; v < V; ++v) {
-    ok[v] = lane + 32 * v < width;
-    bias_r[v] = ok[v] ? bvec[32 * v] : Ops::zero();
-  }
+  for (int v = 0; v < V; ++v) ok[v] = lane + 32 * v < width;
+  const VT* __restrict__ bvec = reinterpret_cast<const VT*>(p.bias) + c0 + lane;
   const VT* __restrict__ Wv = reinterpret_cast<const VT*>(p.W) + c0 + lane;
-  const int64_t row_vec = p.g.n_vec;
+  const int row_vec = p.g.n_vec;
 
   const int64_t n_items = (int64_t)p.P * p.B;
   int64_t item = ((int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5)) * p.items_per_warp;
   const int64_t item_end = item + p.items_per_warp < n_items ? item + p.items_per_warp : n_items;
   if (item >= item_end) return;
-
   auto index_row = [&](int64_t it) {
     const int q = it >= p.B ? 1 : 0;
     return (q ? p.idx[1] : p.idx[0]) + (it - (int64_t)q * p.B) * p.K;
   };
-  const int n_super = (p.K + 32 * kIdxGroups - 1) / (32 * kIdxGroups);  // 1 for K <= 256
-
-  // indices of the first item; later items are prefetched one item ahead
+  const int n_super = (p.K + 32 * kIdxGroups - 1) / (32 * kIdxGroups);
   int f[kIdxGroups];
   load_index_groups(index_row(item), p.K, 0, lane, f);
 
@@ -103,42 +101,33 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
     const int persp = item >= p.B ? 1 : 0;
     const int64_t b = item - (int64_t)persp * p.B;
     const int32_t* __restrict__ irow = index_row(item);
-
     VT acc[V];
 #pragma unroll
-    for (int v = 0; v < V; ++v) acc[v] = bias_r[v];
-
+    for (int v = 0; v < V; ++v) acc[v] = ok[v] ? Ops::ldg(bvec + 32 * v) : Ops::zero();
     for (int sg = 0; sg < n_super; ++sg) {
       if (sg > 0) load_index_groups(irow, p.K, sg * kIdxGroups, lane, f);
-      const int n = compact_valid(f, p.T, list, lane);
-      // prefetch the next item's indices while this item's rows are in flight
+      const int n = compact_valid(f, p.T, list, lane, row_vec);
+      // the next item's indices load while this item's rows are in flight
       if (sg == n_super - 1 && item + 1 < item_end) load_index_groups(index_row(item + 1), p.K, 0, lane, f);
-      // Two batches of U rows in flight: batch i + 1 is issued before batch
-      // i is added, so the warp never drains its loads between batches.
-      VT wa[U][V], wb[U][V];
-      int ra[U], rb[U];
-      auto fetch = [&](int u0, VT (&w)[U][V], int (&r)[U]) {
+      VT w[D][V];
+      auto issue = [&](int slot, int j) {
+        const int off = j < n ? list[j] : -1;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          r[u] = u0 + u < n ? list[u0 + u] : -1;
+        for (int v = 0; v < V; ++v)
+          if (off >= 0 && ok[v]) w[slot][v] = Ops::ldg(Wv + off + 32 * v);
+      };
 #pragma unroll
-          for (int v = 0; v < V; ++v)
-            if (r[u] >= 0 && ok[v]) w[u][v] = Ops::ldg(Wv + (int64_t)r[u] * row_vec + 32 * v);
+      for (int d = 0; d < D; ++d) issue(d, d);
+      for (int j0 = 0; j0 < n; j0 += D) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+          if (j0 + d < n) {
+#pragma unroll
+            for (int v = 0; v < V; ++v)
+              if (ok[v]) Ops::add(acc[v], w[d][v]);
+          }
+          issue(d, j0 + d + D);
         }
-      };
-      auto consume = [&](const VT (&w)[U][V], const int (&r)[U]) {
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-          for (int v = 0; v < V; ++v)
-            if (r[u] >= 0 && ok[v]) Ops::add(acc[v], w[u][v]);
-      };
-      if (n > 0) fetch(0, wa, ra);
-      for (int u0 = 0; u0 < n; u0 += 2 * U) {
-        if (u0 + U < n) fetch(u0 + U, wb, rb);
-        consume(wa, ra);
-        if (u0 + 2 * U < n) fetch(u0 + 2 * U, wa, ra);
-        if (u0 + U < n) consume(wb, rb);
       }
       __syncwarp();  // every lane has read `list` before it is rewritten
     }

@@ -46,14 +46,14 @@ int check_launch(const char* what) {
 }
 
 struct Tuning {
-  int64_t fwd_chunk_vec = 53;       // forward column chunk, in 16-byte vectors
+  int64_t fwd_chunk_vec = 32;       // forward column chunk, in 16-byte vectors
   int64_t fwd_items_per_warp = 16;  // (perspective, position) items per warp
-  int64_t fwd_unroll = 4;          // table rows in flight per warp (4 or 8)
+  int64_t fwd_unroll = 6;          // table rows in flight per warp (4, 6 or 8)
   int64_t bwd_unroll = 4;          // dOut rows per batch, light rows (2, 4 or 8)
   int64_t bwd_entries_per_warp = 2048;  // streaming backward: sorted entries per warp
-  int64_t fwd_min_blocks = 2;      // forward: registers sized for 2, 3 or 4 resident blocks (else compiler's choice)
+  int64_t fwd_min_blocks = 4;      // forward: registers sized for 2..6 resident blocks (chunks <= 64 vectors)
   int64_t bwd_min_blocks = 6;      // light rows: registers sized for 4, 5, 6 or 8 resident blocks (else compiler's)
-  int64_t fwd_exact_chunks = 0;    // 1: full-width chunks + narrow tail; 0: balanced widths
+  int64_t fwd_exact_chunks = 1;    // 1: full-width chunks + narrow tail; 0: balanced widths
   int64_t bwd_exact_chunks = 1;
   int64_t bwd_variant = 1;  // 1: warp per light row (+ heavy-row kernel); 0: streaming
   int64_t bwd_stream_cfg = 0;      // streaming kernel shape (stages / group / warps per block)
@@ -82,7 +82,7 @@ ParamRef* params() {
       {"fwd_exact_chunks", &g_tune.fwd_exact_chunks, 0, 1},
       {"bwd_exact_chunks", &g_tune.bwd_exact_chunks, 0, 1},
       {"bwd_variant", &g_tune.bwd_variant, 0, 1},
-      {"fwd_min_blocks", &g_tune.fwd_min_blocks, 0, 4},
+      {"fwd_min_blocks", &g_tune.fwd_min_blocks, 0, 6},
       {"bwd_min_blocks", &g_tune.bwd_min_blocks, 0, 8},
       {"bwd_stream_cfg", &g_tune.bwd_stream_cfg, 0, 5},
       {"bwd_chunk_vec", &g_tune.bwd_chunk_vec, 0, 1 << 20},
@@ -122,33 +122,35 @@ int lanes_per_row(const Geom& g) { return (g.max_width + 31) / 32; }
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
-template <typename VT, int V, int U>
-void launch_forward_vu(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
+template <typename VT, int V, int D, int MINB>
+void launch_forward_vd(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
   const int64_t n_items = (int64_t)p.P * p.B;
   const int64_t warps = ceil_div(n_items, p.items_per_warp);
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(warps, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
-  if constexpr (V <= 2) {
-    switch (g_tune.fwd_min_blocks) {
-      case 2: ft_forward_kernel<VT, V, U, 2><<<grid, kBlock, 0, s>>>(p); return;
-      case 3: ft_forward_kernel<VT, V, U, 3><<<grid, kBlock, 0, s>>>(p); return;
-      case 4: ft_forward_kernel<VT, V, U, 4><<<grid, kBlock, 0, s>>>(p); return;
-      default: break;
-    }
+  ft_forward_kernel<VT, V, D, MINB><<<grid, kBlock, 0, s>>>(p);
+}
+
+template <typename VT, int V, int D>
+void launch_forward_vd(const FwdParams& p, int chunk0, int n_chunks, cudaStream_t s) {
+  switch (g_tune.fwd_min_blocks) {
+    case 3: launch_forward_vd<VT, V, D, 3>(p, chunk0, n_chunks, s); return;
+    case 4: launch_forward_vd<VT, V, D, 4>(p, chunk0, n_chunks, s); return;
+    case 5: launch_forward_vd<VT, V, D, 5>(p, chunk0, n_chunks, s); return;
+    case 6: launch_forward_vd<VT, V, D, 6>(p, chunk0, n_chunks, s); return;
+    default: launch_forward_vd<VT, V, D, 2>(p, chunk0, n_chunks, s); return;
   }
-  ft_forward_kernel<VT, V, U><<<grid, kBlock, 0, s>>>(p);
 }
 
 template <typename VT, int V>
 void launch_forward_v(const FwdParams& p, int chunk0, int n_chunks, cudaStream_t s) {
   if constexpr (V <= 2) {
-    if (g_tune.fwd_unroll >= 8) launch_forward_vu<VT, V, 8>(p, chunk0, n_chunks, s);
-    else launch_forward_vu<VT, V, 4>(p, chunk0, n_chunks, s);
-  } else if constexpr (V <= 4) {
-    launch_forward_vu<VT, V, 4>(p, chunk0, n_chunks, s);
+    if (g_tune.fwd_unroll >= 8) launch_forward_vd<VT, V, 8>(p, chunk0, n_chunks, s);
+    else if (g_tune.fwd_unroll >= 6) launch_forward_vd<VT, V, 6>(p, chunk0, n_chunks, s);
+    else launch_forward_vd<VT, V, 4>(p, chunk0, n_chunks, s);
   } else {
-    launch_forward_vu<VT, V, 2>(p, chunk0, n_chunks, s);
+    launch_forward_vd<VT, V, 4, 1>(p, chunk0, n_chunks, s);  // wide chunks: compiler's register budget
   }
 }
 
@@ -192,6 +194,8 @@ int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int
   p.g = v4 ? make_geom(C / 4, g_tune.fwd_chunk_vec, g_tune.fwd_exact_chunks)
              : make_geom(C, g_tune.fwd_chunk_vec * 4, g_tune.fwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "forward: column chunk too wide");
+  if (T * (int64_t)p.g.n_vec > INT32_MAX)
+    return fail(NNUE_ERR_UNSUPPORTED, "forward: table exceeds 2^31 %s", v4 ? "16-byte vectors" : "floats");
   if (v4) launch_forward<float4>(p, s);
   else launch_forward<float>(p, s);
   return check_launch("forward");

@@ -101,6 +101,10 @@ def _with_params(params, fn):
         {"sort_tile_rows": 1, "sort_tile": 512},
         {"sort_tile_rows": 7, "sort_tile": 1536},
         {"colsum_parts": 1},
+        {"bwd_unroll": 2, "bwd_min_blocks": 8},
+        {"bwd_unroll": 8, "bwd_min_blocks": 4},
+        {"bwd_unroll": 4, "bwd_min_blocks": 0},
+        {"bwd_unroll": 4, "bwd_min_blocks": 5, "bwd_chunk_vec": 64, "bwd_exact_chunks": 1},
     ],
 )
 def test_backward_tuning_and_heavy_rows(cuda, params):

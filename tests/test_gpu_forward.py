@@ -79,20 +79,36 @@ def test_forward_empty_rows_and_batches(cuda):
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("chunk,ipw", [(0, 1), (16, 2), (32, 4), (64, 4), (128, 16), (8, 3), (100, 5), (300, 2)])
-def test_forward_tuning_variants_bit_exact(cuda, chunk, ipw):
+@pytest.mark.parametrize(
+    "params",
+    [
+        {"fwd_chunk_vec": 0, "fwd_items_per_warp": 1},
+        {"fwd_chunk_vec": 16, "fwd_items_per_warp": 2},
+        {"fwd_chunk_vec": 32, "fwd_items_per_warp": 4},
+        {"fwd_chunk_vec": 64, "fwd_items_per_warp": 4},
+        {"fwd_chunk_vec": 128, "fwd_items_per_warp": 16},
+        {"fwd_chunk_vec": 8, "fwd_items_per_warp": 3},
+        {"fwd_chunk_vec": 100, "fwd_items_per_warp": 5},
+        {"fwd_chunk_vec": 300, "fwd_items_per_warp": 2},
+        {"fwd_chunk_vec": 53, "fwd_exact_chunks": 0, "fwd_unroll": 4, "fwd_min_blocks": 3},
+        {"fwd_unroll": 8, "fwd_min_blocks": 2},
+        {"fwd_unroll": 4, "fwd_min_blocks": 6},
+        {"fwd_unroll": 6, "fwd_min_blocks": 5, "fwd_items_per_warp": 7},
+    ],
+)
+def test_forward_tuning_variants_bit_exact(cuda, params):
     white, _, T = feature_batch(400, "Full_Threats+HalfKAv2_hm^", seed=12)
     C = 1048
     W = random_table(T, C, seed=13)
     bias = random_table(1, C, seed=14)[0]
-    old = (_native.get_param("fwd_chunk_vec"), _native.get_param("fwd_items_per_warp"))
+    old = {k: _native.get_param(k) for k in params}
     try:
-        _native.set_param("fwd_chunk_vec", chunk)
-        _native.set_param("fwd_items_per_warp", ipw)
+        for k, v in params.items():
+            _native.set_param(k, v)
         got = _fwd(white, W, bias, cuda)
     finally:
-        _native.set_param("fwd_chunk_vec", old[0])
-        _native.set_param("fwd_items_per_warp", old[1])
+        for k, v in old.items():
+            _native.set_param(k, v)
     np.testing.assert_array_equal(got, oracle.ft_forward(white, W, bias))
 
 

@@ -339,6 +339,239 @@ __global__ void __launch_bounds__(kBlock) sort_scatter_kernel(const PassParams p
   }
 }
 
+// ----------------------------------------------------------------------------
+// Counting placement (sort_variant 1): the same (key -> ascending b) lists as
+// the radix passes, built as a sparse transpose.
+//   count : one pass over the raw index arrays, seg[key] += 1 per valid slot
+//   scan  : exclusive scan -> seg_start; cursor = copy of seg_start
+//   place : second pass; slot = atomicAdd(cursor[key], 1), values land in
+//           their key's segment in arbitrary order
+//   order : every segment is sorted ascending (values of one key share the
+//           perspective, so ascending value = ascending b).  Equal values are
+//           the same position twice, so the order among them cannot change
+//           any sum; the result equals the stable radix sort.
+//           n <= 256: one warp, bitonic network in registers;
+//           n <= kSegSmem: one block, bitonic network in shared memory;
+//           larger: one block counts positions in shared-memory windows.
+// ----------------------------------------------------------------------------
+// The raw slots of perspective q, four at a time when aligned.
+struct RawCursor {
+  const int32_t* base;
+  int64_t n;
+  bool vec4;
+};
+
+__device__ __forceinline__ RawCursor raw_cursor(const RawSrc& r, int q) {
+  const int32_t* b = q ? r.idx[1] : r.idx[0];
+  return RawCursor{b, r.n_raw, (reinterpret_cast<uintptr_t>(b) & 15) == 0};
+}
+
+// Calls fn(e, f) for every slot e of perspective q in this thread's share.
+template <typename Fn>
+__device__ __forceinline__ void for_raw_slots(const RawCursor& c, int64_t tid, int64_t nthreads, Fn&& fn) {
+  if (c.vec4) {
+    const int64_t n4 = c.n >> 2;
+    const int4* b4 = reinterpret_cast<const int4*>(c.base);
+    for (int64_t i = tid; i < n4; i += nthreads) {
+      const int4 v = __ldcs(b4 + i);
+      fn(4 * i, v.x);
+      fn(4 * i + 1, v.y);
+      fn(4 * i + 2, v.z);
+      fn(4 * i + 3, v.w);
+    }
+    for (int64_t e = 4 * n4 + tid; e < c.n; e += nthreads) fn(e, __ldcs(c.base + e));
+  } else {
+    for (int64_t e = tid; e < c.n; e += nthreads) fn(e, __ldcs(c.base + e));
+  }
+}
+
+__global__ void __launch_bounds__(kBlock) count_keys_kernel(const RawSrc r, int32_t* __restrict__ seg) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int q = 0; q < r.P; ++q) {
+    const RawCursor c = raw_cursor(r, q);
+    for_raw_slots(c, tid, nthreads, [&](int64_t, int f) {
+      if ((unsigned)f < (unsigned)r.T) atomicAdd(seg + (int64_t)f * r.P + q, 1);
+      else if (f != -1) flag_error(kErrBadIndex);
+    });
+  }
+}
+
+__global__ void __launch_bounds__(kBlock) place_keys_kernel(const RawSrc r, int32_t* __restrict__ cursor,
+                                                           int32_t* __restrict__ vals, int64_t cap) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  const int64_t B = r.K > 0 ? r.n_raw / r.K : 0;
+  for (int q = 0; q < r.P; ++q) {
+    const RawCursor c = raw_cursor(r, q);
+    for_raw_slots(c, tid, nthreads, [&](int64_t e, int f) {
+      if ((unsigned)f >= (unsigned)r.T) return;
+      const int pos = atomicAdd(cursor + (int64_t)f * r.P + q, 1);
+      if ((unsigned long long)(unsigned)pos < (unsigned long long)cap) vals[pos] = (int)(q * B + e / r.K);
+      else flag_error(kErrBadSegment);
+    });
+  }
+}
+
+// Ascending bitonic sort of the n <= 32 * E values at data[0, n), one warp,
+// blocked layout (lane l holds elements l * E .. l * E + E - 1).
+template <int E>
+__device__ __forceinline__ void warp_sort_segment(int32_t* __restrict__ data, int n, int lane) {
+  constexpr int N = 32 * E;
+  int v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = lane * E + e;
+    v[e] = i < n ? data[i] : INT32_MAX;
+  }
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= E) {  // partner element in lane ^ (j / E), same slot
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int i = lane * E + e;
+          const int other = __shfl_xor_sync(kFull, v[e], j / E);
+          const bool up = (i & k) == 0, lower = (i & j) == 0;
+          v[e] = (lower == up) ? min(v[e], other) : max(v[e], other);
+        }
+      } else {  // partner slot e ^ j in this lane
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          if (e & j) continue;
+          const bool up = ((lane * E + e) & k) == 0;
+          const int a = v[e], b = v[e ^ j];
+          v[e] = up ? min(a, b) : max(a, b);
+          v[e ^ j] = up ? max(a, b) : min(a, b);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = lane * E + e;
+    if (i < n) data[i] = v[e];
+  }
+}
+
+// One warp per key: segments of <= 256 values are sorted here, longer ones
+// are listed for order_big_segments_kernel (big[0] = count, big[1..] = keys).
+__global__ void __launch_bounds__(kBlock) order_segments_kernel(const int32_t* __restrict__ seg, int64_t NK,
+                                                               int32_t* __restrict__ vals, int32_t* __restrict__ big) {
+  const int lane = threadIdx.x & 31;
+  const int64_t key = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (key >= NK) return;
+  const int s = seg[key], n = seg[key + 1] - s;
+  if (n <= 1) return;
+  if (n <= 32) {
+    // placement often leaves short segments in order already
+    const int v = lane < n ? vals[s + lane] : INT32_MAX;
+    const int next = __shfl_down_sync(kFull, v, 1);
+    if (__all_sync(kFull, lane >= n - 1 || v <= next)) return;
+  }
+  if (n <= 32) warp_sort_segment<1>(vals + s, n, lane);
+  else if (n <= 64) warp_sort_segment<2>(vals + s, n, lane);
+  else if (n <= 128) warp_sort_segment<4>(vals + s, n, lane);
+  else if (n <= 256) warp_sort_segment<8>(vals + s, n, lane);
+  else if (lane == 0) big[1 + atomicAdd(big, 1)] = (int32_t)key;
+}
+
+constexpr int kSegSmem = 8192;      // values sorted in shared memory by one block
+constexpr int kSegWindow = 16384;   // positions counted per window (16-bit counters, two per word)
+constexpr int kBigThreads = 512;
+
+// One block per long segment.  Either a bitonic network over the values in
+// shared memory, or a counting sort by position, kSegWindow positions per
+// window (the values of one key lie in [v0, v0 + B)); the cheaper one by
+// operation count is taken.  The count reads a copy of the segment in
+// `spare` (an int array as long as `vals`).  Counters are 16-bit: the host
+// only selects this path when max_active < 65536, so no (key, position)
+// pair can repeat more often.
+__global__ void __launch_bounds__(kBigThreads) order_big_segments_kernel(const int32_t* __restrict__ seg,
+                                                                        int32_t P, int64_t B,
+                                                                        int32_t* __restrict__ vals,
+                                                                        int32_t* __restrict__ spare,
+                                                                        const int32_t* __restrict__ big) {
+  __shared__ uint32_t sm[kSegSmem > kSegWindow / 2 ? kSegSmem : kSegWindow / 2];
+  __shared__ int scratch[33];
+  const int n_big = big[0];
+  const int64_t windows = (B + kSegWindow - 1) / kSegWindow;
+  for (int bi = blockIdx.x; bi < n_big; bi += gridDim.x) {
+    const int64_t key = big[1 + bi];
+    const int s = seg[key], n = seg[key + 1] - s;
+    int32_t* d = vals + s;
+    int N = 1, lg = 0;
+    while (N < n) {
+      N <<= 1;
+      ++lg;
+    }
+    const bool network = n <= kSegSmem && (int64_t)lg * (lg + 1) / 2 * N < windows * ((int64_t)n + kSegWindow);
+    if (network) {
+      int32_t* si = reinterpret_cast<int32_t*>(sm);
+      for (int i = threadIdx.x; i < N; i += blockDim.x) si[i] = i < n ? d[i] : INT32_MAX;
+      __syncthreads();
+      for (int k = 2; k <= N; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          for (int i = threadIdx.x; i < N; i += blockDim.x) {
+            const int x = i ^ j;
+            if (x > i) {
+              const int a = si[i], b = si[x];
+              const bool up = (i & k) == 0;
+              if ((a > b) == up) {
+                si[i] = b;
+                si[x] = a;
+              }
+            }
+          }
+          __syncthreads();
+        }
+      for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = si[i];
+    } else {
+      int32_t* src = spare + s;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) src[i] = d[i];
+      __syncthreads();
+      const int64_t v0 = (key % P) * B;
+      int out = 0;
+      for (int64_t w0 = 0; w0 < B; w0 += kSegWindow) {
+        for (int i = threadIdx.x; i < kSegWindow / 2; i += blockDim.x) sm[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+          const int64_t b = (int64_t)src[i] - v0 - w0;
+          if (b >= 0 && b < kSegWindow) atomicAdd(&sm[b >> 1], 1u << (16 * (int)(b & 1)));
+        }
+        __syncthreads();
+        constexpr int kWords = kSegWindow / 2 / kBigThreads;  // counter words per thread
+        uint32_t c[kWords];
+        int tsum = 0;
+#pragma unroll
+        for (int t = 0; t < kWords; ++t) {
+          c[t] = sm[threadIdx.x * kWords + t];
+          tsum += (int)(c[t] & 0xffffu) + (int)(c[t] >> 16);
+        }
+        const int incl = block_inclusive_scan(tsum, scratch);
+        const int total = scratch[32];
+        int o = out + incl - tsum;
+#pragma unroll
+        for (int t = 0; t < kWords; ++t) {
+          const int value = (int)(v0 + w0 + 2 * (threadIdx.x * kWords + t));
+          const int c0 = (int)(c[t] & 0xffffu), c1 = (int)(c[t] >> 16);
+          for (int r = 0; r < c0; ++r)
+            if (o + r < n) d[o + r] = value;
+          o += c0;
+          for (int r = 0; r < c1; ++r)
+            if (o + r < n) d[o + r] = value + 1;
+          o += c1;
+        }
+        out += total;
+        __syncthreads();
+      }
+      if (out != n && threadIdx.x == 0) flag_error(kErrBadSegment);
+    }
+    __syncthreads();
+  }
+}
+
 // Rows with more than `threshold` entries (both perspectives) are heavy
 // (used by the fallback walk path only).
 __global__ void classify_rows_kernel(const int32_t* __restrict__ seg_start, int32_t T, int32_t P,

@@ -62,6 +62,8 @@ struct Tuning {
   int64_t heavy_cap = 512;         // at most this many heavy rows per call
   int64_t sort_tile_rows = 32;     // index rows (positions) per warp in the first sort pass
   int64_t sort_tile = 1024;        // entries per warp in later sort passes
+  int64_t sort_variant = 1;        // 1: counting placement + per-segment sort, 0: LSD radix passes
+  int64_t sort_blocks_per_sm = 16;  // counting placement: grid of the two passes over the index arrays
   int64_t colsum_parts = 296;      // position ranges of the bias column sum
 };
 Tuning g_tune;
@@ -89,6 +91,8 @@ ParamRef* params() {
       {"heavy_threshold", &g_tune.heavy_threshold, 1, int64_t(1) << 40},
       {"heavy_cap", &g_tune.heavy_cap, 0, 1 << 24},
       {"sort_tile_rows", &g_tune.sort_tile_rows, 1, 1 << 16},
+      {"sort_variant", &g_tune.sort_variant, 0, 1},
+      {"sort_blocks_per_sm", &g_tune.sort_blocks_per_sm, 1, 1 << 16},
       {"sort_tile", &g_tune.sort_tile, 32 * kSortBatch, 1 << 20},
       {"colsum_parts", &g_tune.colsum_parts, 1, 1 << 16},
       {nullptr, nullptr, 0, 0},
@@ -211,8 +215,10 @@ struct BwdPlan {
   int dbits[3] = {0, 0, 0}, shift[3] = {0, 0, 0};
   int64_t tile_raw = 0, tile = 0, tiles_raw = 0, tiles_max = 0, hist_len = 0, scan_blocks = 0;
   int64_t heavy_cap = 0, heavy_threshold = 0, parts = 0, epw = 0, n_stream_warps = 0;
+  int sort_variant = 0;
   size_t off_seg = 0, off_hist = 0, off_bsum = 0, off_ka = 0, off_va = 0, off_kb = 0, off_vb = 0;
-  size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, off_first = 0, total = 0;
+  size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, off_first = 0, off_cursor = 0, off_big = 0;
+  size_t total = 0;
 };
 
 int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl) {
@@ -251,6 +257,7 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
   pl.parts = std::max<int64_t>(1, std::min<int64_t>(g_tune.colsum_parts, B));
   pl.epw = g_tune.bwd_entries_per_warp;
   pl.n_stream_warps = pl.nnz_max / pl.epw + 1;
+  pl.sort_variant = K < 65536 ? (int)g_tune.sort_variant : 0;  // 16-bit position counters
   const int64_t n_vec_floats = C;  // float64 partial column sums
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -259,17 +266,19 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
     return at;
   };
   pl.off_seg = take(sizeof(int32_t) * (pl.NK + 1));
-  pl.off_hist = take(sizeof(int32_t) * pl.hist_len);
+  pl.off_hist = take(pl.sort_variant == 1 ? 0 : sizeof(int32_t) * pl.hist_len);
   pl.off_bsum = take(sizeof(int32_t) * (pl.scan_blocks + 1));
   pl.off_ka = take(sizeof(int32_t) * pl.nnz_max);
   pl.off_va = take(sizeof(int32_t) * pl.nnz_max);
-  pl.off_kb = take(pl.npass >= 3 ? sizeof(int32_t) * pl.nnz_max : 0);
-  pl.off_vb = take(pl.npass >= 2 ? sizeof(int32_t) * pl.nnz_max : 0);
+  pl.off_kb = take(pl.npass >= 3 && pl.sort_variant == 0 ? sizeof(int32_t) * pl.nnz_max : 0);
+  pl.off_vb = take(pl.npass >= 2 && pl.sort_variant == 0 ? sizeof(int32_t) * pl.nnz_max : 0);
   pl.off_nheavy = take(sizeof(int32_t));
   pl.off_heavy = take(sizeof(int32_t) * pl.heavy_cap);
   pl.off_kind = take(sizeof(uint8_t) * T);
   pl.off_partial = take(sizeof(double) * P * pl.parts * n_vec_floats);
   pl.off_first = take(sizeof(int32_t) * (pl.n_stream_warps + 1));
+  pl.off_cursor = take(pl.sort_variant == 1 ? sizeof(int32_t) * pl.NK : 0);
+  pl.off_big = take(pl.sort_variant == 1 ? sizeof(int32_t) * (pl.NK + 1) : 0);
   pl.total = o;
   return NNUE_OK;
 }
@@ -279,6 +288,7 @@ struct Ws {
   uint8_t* kind;
   double* partial;
   int32_t* first_row;
+  int32_t *cursor, *big;
 };
 
 Ws carve(const BwdPlan& pl, void* base) {
@@ -296,11 +306,15 @@ Ws carve(const BwdPlan& pl, void* base) {
   w.kind = reinterpret_cast<uint8_t*>(b + pl.off_kind);
   w.partial = reinterpret_cast<double*>(b + pl.off_partial);
   w.first_row = reinterpret_cast<int32_t*>(b + pl.off_first);
+  w.cursor = reinterpret_cast<int32_t*>(b + pl.off_cursor);
+  w.big = reinterpret_cast<int32_t*>(b + pl.off_big);
   return w;
 }
 
 // sorted position list = values written by the last pass
-const int32_t* sorted_values(const BwdPlan& pl, const Ws& w) { return (pl.npass % 2 == 1) ? w.va : w.vb; }
+const int32_t* sorted_values(const BwdPlan& pl, const Ws& w) {
+  return (pl.sort_variant == 1 || pl.npass % 2 == 1) ? w.va : w.vb;
+}
 
 void run_scan(int32_t* data, ScanLen L, int64_t max_len, int32_t* bsum, cudaStream_t s) {
   const int64_t nb = ceil_div(max_len, kScanTile);
@@ -324,7 +338,25 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
   raw.K = pl.K;
   raw.T = (int32_t)pl.T;
   raw.P = pl.P;
-  for (int i = 0; i < pl.npass; ++i) {
+  if (pl.sort_variant == 1) {
+    if (cudaMemsetAsync(w.big, 0, sizeof(int32_t), s) != cudaSuccess)
+      return check_launch("backward_prepare: memset");
+    const unsigned grid = (unsigned)std::max<int64_t>(
+        1, std::min<int64_t>(ceil_div(raw.n_raw, 4 * kBlock), 148 * g_tune.sort_blocks_per_sm));
+    count_launch();
+    count_keys_kernel<<<grid, kBlock, 0, s>>>(raw, w.seg);
+    run_scan(w.seg, ScanLen{pl.NK + 1, nullptr, 0, 0}, pl.NK + 1, w.bsum, s);
+    if (cudaMemcpyAsync(w.cursor, w.seg, sizeof(int32_t) * pl.NK, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return check_launch("backward_prepare: cursor copy");
+    count_launch();
+    place_keys_kernel<<<grid, kBlock, 0, s>>>(raw, w.cursor, w.va, pl.nnz_max);
+    count_launch();
+    order_segments_kernel<<<(unsigned)ceil_div(pl.NK, kWarpsPerBlock), kBlock, 0, s>>>(w.seg, pl.NK, w.va, w.big);
+    count_launch();
+    order_big_segments_kernel<<<(unsigned)std::min<int64_t>(pl.NK, 2 * 148), kBigThreads, 0, s>>>(
+        w.seg, pl.P, pl.B, w.va, w.ka, w.big);
+  }
+  for (int i = 0; i < (pl.sort_variant == 1 ? 0 : pl.npass); ++i) {
     const bool first = i == 0, last = i == pl.npass - 1;
     PassParams pp{};
     pp.raw = raw;

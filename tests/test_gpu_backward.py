@@ -1,4 +1,4 @@
-"""Backward (device radix CSR + segment sums + bias column sum) vs the oracle.
+"""Backward (device CSR build + segment sums + bias column sum) vs the oracle.
 
 dW is bit-exact: each feature's sum runs over positions in ascending order,
 like the reference's stable sort + sequential segment kernel, and the two
@@ -19,6 +19,16 @@ from _inputs import feature_batch, random_indices, random_table
 pytestmark = pytest.mark.gpu
 
 RTOL, ATOL = 1e-5, 1e-6
+
+
+@pytest.fixture(autouse=True, params=[0, 1], ids=["radix", "counting"])
+def sort_variant(request):
+    """Every test runs with both index phases: LSD radix passes, and counting
+    placement + per-segment sort."""
+    old = _native.get_param("sort_variant")
+    _native.set_param("sort_variant", request.param)
+    yield request.param
+    _native.set_param("sort_variant", old)
 
 
 def _grads(B, C, seed):
@@ -219,3 +229,22 @@ def test_forward_pair_prepare_then_apply(cuda):
     rW, rB = oracle.ft_backward_pair(white, black, g0, g1, T)
     np.testing.assert_array_equal(dW.cpu().numpy(), rW)
     np.testing.assert_allclose(dB.cpu().numpy(), rB, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("B,T", [(5000, 50), (9000, 50), (20000, 50), (40000, 500)])
+def test_backward_long_segments(cuda, B, T):
+    """Segments longer than one warp's sort (256) and than one block's shared
+    memory (8192), with repeated positions inside a segment; counted in one
+    or several position windows, or (B = 40000: ~320 per key) sorted by the
+    block network."""
+    C, K = 8, 4
+    i0 = random_indices(B, K, T, seed=41)
+    i1 = random_indices(B, K, T, seed=42)
+    i0[:, 0] = 7  # every position
+    i0[::3, 1] = 7  # a third of them twice
+    i1[:, 2] = 7
+    g0, g1 = _grads(B, C, 43)
+    dW, dB = _bwd_pair(i0, i1, g0, g1, T, cuda)
+    rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
+    np.testing.assert_array_equal(dW, rW)
+    np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)

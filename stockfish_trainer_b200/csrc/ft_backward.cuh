@@ -663,36 +663,63 @@ __device__ __forceinline__ void seg_write(const SegParams& p, int64_t f, int col
   }
 }
 
+// Row offset (in vectors) of the position stored in a sorted value of
+// perspective q: (v - q * B) * row_vec.  Values outside the perspective's
+// range (a corrupt workspace) are flagged and read row 0 instead, so every
+// load stays in bounds.  The host guarantees B * row_vec < 2^31.
+__device__ __forceinline__ int position_offset(int v, int q, int64_t B, int row_vec) {
+  int b = v - q * (int)B;
+  if ((unsigned)b >= (unsigned)B) {
+    flag_error(kErrBadSegment);
+    b = 0;
+  }
+  return b * row_vec;
+}
+
 // acc[v] += dOut_q[b, cols] for the entries of sorted_b[s, e) (perspective q),
-// ascending, where `my` already holds the decoded first 32 positions
-// (lane i: entry s + i).  Later groups of 32 are loaded as needed.
+// ascending, where `my` already holds the row offsets of the first 32
+// entries (lane i: entry s + i).  Later groups of 32 are loaded as needed.
+// Full batches of U entries run without per-entry checks; only the last
+// batch of a group is predicated.
 template <typename VT, int V, int U>
-__device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src, int64_t row_vec,
-                                                  const int32_t* __restrict__ sb, int s, int e, int q, int64_t B,
-                                                  int my, const bool (&ok)[V], int lane) {
+__device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src, int row_vec,
+                                        const int32_t* __restrict__ sb, int s, int e, int q, int64_t B, int my,
+                                        const bool (&ok)[V], int lane) {
   using Ops = Vec<VT>;
   for (int j0 = s; j0 < e; j0 += 32) {
     const int cnt = e - j0 < 32 ? e - j0 : 32;
-    if (j0 != s) my = lane < cnt ? decode_position(__ldg(sb + j0 + lane), q, B) : -1;
-    for (int u0 = 0; u0 < cnt; u0 += U) {
-      int rows[U];
-      bool has[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        rows[u] = __shfl_sync(kFull, my, (u0 + u) & 31);
-        has[u] = u0 + u < cnt && rows[u] >= 0;
-      }
+    if (j0 != s) my = lane < cnt ? position_offset(__ldg(sb + j0 + lane), q, B, row_vec) : 0;
+    int u0 = 0;
+#pragma unroll 1
+    for (; u0 + U <= cnt; u0 += U) {
       VT w[U][V];
 #pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int o = __shfl_sync(kFull, my, u0 + u);
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (ok[v]) w[u][v] = Ops::ldg(src + o + 32 * v);
+      }
+#pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int v = 0; v < V; ++v)
-          if (has[u] && ok[v]) w[u][v] = Ops::ldg(src + (int64_t)rows[u] * row_vec + 32 * v);
+          if (ok[v]) Ops::add(acc[v], w[u][v]);
+    }
+    if (u0 < cnt) {
+      VT w[U][V];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int o = __shfl_sync(kFull, my, (u0 + u) & 31);
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (u0 + u < cnt && ok[v]) w[u][v] = Ops::ldg(src + o + 32 * v);
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int v = 0; v < V; ++v)
-          if (has[u] && ok[v]) Ops::add(acc[v], w[u][v]);
+          if (u0 + u < cnt && ok[v]) Ops::add(acc[v], w[u][v]);
     }
   }
 }
@@ -713,7 +740,7 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_segsum_light_kernel(const Seg
   const int chunk = p.chunk0 + blockIdx.y;
   const int c0 = p.g.begin(chunk);
   const int width = p.g.width(chunk);
-  const int64_t row_vec = p.g.n_vec;
+  const int row_vec = p.g.n_vec;
   const int64_t f = p.row_begin + (int64_t)blockIdx.x * kWarpsPerBlock + warp;
   if (f >= p.row_end) return;
   const int P = p.P;
@@ -723,8 +750,8 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_segsum_light_kernel(const Seg
   const int s1 = __shfl_sync(kFull, bnd, 1);
   const int e1 = __shfl_sync(kFull, bnd, P);
   if (kind) return;
-  const int g0 = s0 + lane < s1 ? decode_position(__ldg(p.sorted_b + s0 + lane), 0, p.B) : -1;
-  const int g1 = (P == 2 && s1 + lane < e1) ? decode_position(__ldg(p.sorted_b + s1 + lane), 1, p.B) : -1;
+  const int g0 = s0 + lane < s1 ? position_offset(__ldg(p.sorted_b + s0 + lane), 0, p.B, row_vec) : 0;
+  const int g1 = (P == 2 && s1 + lane < e1) ? position_offset(__ldg(p.sorted_b + s1 + lane), 1, p.B, row_vec) : 0;
   bool ok[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) ok[v] = lane + 32 * v < width;

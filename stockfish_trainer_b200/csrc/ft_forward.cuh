@@ -118,7 +118,21 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
       };
 #pragma unroll
       for (int d = 0; d < D; ++d) issue(d, d);
-      for (int j0 = 0; j0 < n; j0 += D) {
+      int j0 = 0;
+      // steady state: every slot consumed and re-issued in range, no checks
+      for (; j0 + 2 * D <= n; j0 += D) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+#pragma unroll
+          for (int v = 0; v < V; ++v)
+            if (ok[v]) Ops::add(acc[v], w[d][v]);
+          const int off = list[j0 + d + D];
+#pragma unroll
+          for (int v = 0; v < V; ++v)
+            if (ok[v]) w[d][v] = Ops::ldg(Wv + off + 32 * v);
+        }
+      }
+      for (; j0 < n; j0 += D) {
 #pragma unroll
         for (int d = 0; d < D; ++d) {
           if (j0 + d < n) {

@@ -49,10 +49,10 @@ struct Tuning {
   int64_t fwd_chunk_vec = 32;       // forward column chunk, in 16-byte vectors
   int64_t fwd_items_per_warp = 16;  // (perspective, position) items per warp
   int64_t fwd_unroll = 6;          // table rows in flight per warp (4, 6 or 8)
-  int64_t bwd_unroll = 4;          // dOut rows per batch, light rows (2, 4 or 8)
+  int64_t bwd_unroll = 2;          // dOut rows per batch, light rows (2, 4 or 8)
   int64_t bwd_entries_per_warp = 2048;  // streaming backward: sorted entries per warp
   int64_t fwd_min_blocks = 4;      // forward: registers sized for 2..6 resident blocks (chunks <= 64 vectors)
-  int64_t bwd_min_blocks = 6;      // light rows: registers sized for 4, 5, 6 or 8 resident blocks (else compiler's)
+  int64_t bwd_min_blocks = 8;      // light rows: registers sized for 4, 5, 6 or 8 resident blocks (else compiler's)
   int64_t fwd_exact_chunks = 1;    // 1: full-width chunks + narrow tail; 0: balanced widths
   int64_t bwd_exact_chunks = 1;
   int64_t bwd_variant = 1;  // 1: warp per light row (+ heavy-row kernel); 0: streaming
@@ -138,7 +138,8 @@ void launch_forward_vd(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
 
 template <typename VT, int V, int D>
 void launch_forward_vd(const FwdParams& p, int chunk0, int n_chunks, cudaStream_t s) {
-  switch (g_tune.fwd_min_blocks) {
+  // two vectors per lane need twice the registers: cap their budget at 3 blocks
+  switch (V == 1 ? g_tune.fwd_min_blocks : std::min<int64_t>(g_tune.fwd_min_blocks, 3)) {
     case 3: launch_forward_vd<VT, V, D, 3>(p, chunk0, n_chunks, s); return;
     case 4: launch_forward_vd<VT, V, D, 4>(p, chunk0, n_chunks, s); return;
     case 5: launch_forward_vd<VT, V, D, 5>(p, chunk0, n_chunks, s); return;
@@ -415,7 +416,8 @@ void launch_segsum_vu(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
   dim3 grid((unsigned)ceil_div(p.row_end - p.row_begin, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
   if constexpr (V <= 2) {
-    switch (g_tune.bwd_min_blocks) {
+    // two vectors per lane need twice the registers: cap their budget at 4 blocks
+    switch (V == 1 ? g_tune.bwd_min_blocks : std::min<int64_t>(g_tune.bwd_min_blocks, 4)) {
       case 4: ft_segsum_light_kernel<VT, V, U, 4><<<grid, kBlock, 0, s>>>(p); return;
       case 5: ft_segsum_light_kernel<VT, V, U, 5><<<grid, kBlock, 0, s>>>(p); return;
       case 6: ft_segsum_light_kernel<VT, V, U, 6><<<grid, kBlock, 0, s>>>(p); return;
@@ -582,6 +584,9 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec, g_tune.bwd_exact_chunks)
              : make_geom(pl.C, g_tune.bwd_chunk_vec * 4, g_tune.bwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "backward: column chunk too wide");
+  if (pl.B * (int64_t)p.g.n_vec > INT32_MAX)
+    return fail(NNUE_ERR_UNSUPPORTED, "backward: grad_output exceeds 2^31 %s per perspective",
+                v4 ? "16-byte vectors" : "floats");
 
   const bool full_range = row_begin == 0 && row_end == pl.T;
   const bool stream = v4 && g_tune.bwd_variant == 0 && lanes_per_row(p.g) <= 2 && full_range;

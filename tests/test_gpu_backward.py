@@ -248,3 +248,4 @@ def test_backward_long_segments(cuda, B, T):
     rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
     np.testing.assert_array_equal(dW, rW)
     np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
+

@@ -54,7 +54,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe"], default="headline",
+    p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe", "ranger22"],
+                   default="headline",
                    help="headline: BASELINE configs[2]/[3] (the driver's metric); halfka: configs[1] "
                         "(HalfKAv2_hm^, B=16384, phases reported separately); quantized: configs[4] "
                         "(int16 forward, HalfKAv2_hm^, B=65536); gather-probe: random-row gather bandwidth "
@@ -576,6 +577,72 @@ def run_quantized(args):
     return 0
 
 
+def run_ranger22(args):
+    """Ranger22 step of the FT parameters: the merged
+    85296 x 1048 table and the 1048 bias, each one fused update per step,
+    the lookahead blend fused into every 5th step as in training.  One step =
+    Ranger22FT.step() over both parameters."""
+    import torch
+
+    from oracle import ranger22 as oracle_r22
+    from stockfish_trainer_b200 import _native, optim, positions
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T = positions.feature_set_info(args.feature_set)[1]
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    w = torch.nn.Parameter(torch.randn(T, C, device=dev, generator=gen) * 0.01)
+    b = torch.nn.Parameter(torch.zeros(C, device=dev))
+    w.grad = torch.randn(T, C, device=dev, generator=gen) * 1e-3
+    b.grad = torch.randn(C, device=dev, generator=gen) * 1e-3
+    opt = optim.Ranger22FT([{"params": [w, b]}], lr=8.75e-4, betas=(0.9, 0.999), eps=1.0e-7)
+    for _ in range(max(args.warmup, 3)):
+        opt.step()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count()
+    steps = max(args.steps, 5)
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        opt.step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(e) / steps
+    n = w.numel() + b.numel()
+    merges = sum(1 for k in range(steps) if (max(args.warmup, 3) + k + 1) % 5 == 0)
+    a_bytes = (32 * n * steps + 8 * n * merges) / steps  # p, g, v, m, m_prev read; p, v, m written (+ lookahead)
+    peak, src = hbm_peak()
+    # CPU baseline: the numpy oracle on 2048 rows of the table, scaled to the full table
+    rows = 2048
+    rng = np.random.default_rng(args.seed)
+    pc = (rng.standard_normal((rows, C)) * 0.01).astype(np.float32)
+    gc = (rng.standard_normal((rows, C)) * 1e-3).astype(np.float32)
+    vc, mc, mpc = (np.zeros_like(pc) for _ in range(3))
+    sc = oracle_r22.scalars(8.75e-4, 5)
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        oracle_r22.update(pc, gc, vc, mc, mpc, sc)
+    cpu_s = (time.perf_counter() - t0) / reps * (T / rows)
+    emit({
+        "metric": "FT Ranger22 steps/s (85296x1048 table + bias, fused update, lookahead every 5th step)",
+        "value": 1e3 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: W~N(0,0.01), grad~N(0,1e-3), zero-initialised optimizer state",
+        "config": {"workload": "Ranger22 (trainer configuration) step of the FT table and bias, one fused kernel "
+                               "per parameter", "rows": T, "cols": C, "lookahead_mergetime": 5,
+                   "l2": "parameter and state larger than L2 (2.9 GB per step), no flush"},
+        "roofline": {"bound": "hbm", "achieved": a_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": a_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
+                     "kernel": "ranger22_rows_kernel", "algorithmic_bytes": a_bytes,
+                     "peak_source": f"{src} hbm_gbs"},
+        "cpu_baseline": {"value": 1.0 / cpu_s, "unit": "steps/s", "cores": 1, "kind": "port",
+                         "sample": f"numpy oracle update of {rows} table rows, scaled to {T} rows"},
+        "gpu_launches": int(_native.launch_count() - l0),
+    })
+    return 0
+
+
 _JSON_FD = None
 
 
@@ -599,6 +666,8 @@ def main():
     os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "ranger22":
+        return run_ranger22(args)
     if args.workload == "quantized":
         return run_quantized(args)
     if args.workload == "gather-probe":

@@ -196,6 +196,24 @@ int nnue_ft_halfka_export_quantize(const float *weight, const float *virtual_wei
  * quantize.py:83). */
 int nnue_ft_quantize_i16(const float *x, int64_t n, float scale, int16_t *q, void *stream);
 
+/* ---- Ranger22 parameter update ------------------------------------------
+ * Replaces, for one fp32 parameter, the update of Ranger22.step's fused path
+ * (src/ranger22/optimizer.py:48-107 _compiled_full_update_{1d,2d}, eager twin
+ * :256-301) and, when lookahead_merge != 0, the lookahead blend of that step
+ * (:569-597, torch._foreach_lerp_(p, lookahead, 1 - alpha) then
+ * lookahead = p).  One pass: p, variance_ma and gma_cur are updated in place
+ * (and lookahead on merge steps); grad and gma_prev are read.
+ *   rows x cols: a 2-D parameter takes its norm per row (dim = 1); a 1-D
+ *   parameter is passed as rows = 1 (norm over the whole vector).
+ *   scalars: 12 host floats in the reference's order (optimizer.py:211-245):
+ *   lr, inv_sqrt_bc2, eps, two_nl_factor, noise_norm_recip, pnm_a, pnm_b,
+ *   step_size, beta2, 1 - beta2, beta1^2, 1 - beta1^2.
+ * All device pointers are contiguous fp32 [rows, cols]; nothing is allocated
+ * and nothing synchronises the host. */
+int nnue_ft_ranger22_step(float *param, const float *grad, float *variance_ma, float *gma_cur, const float *gma_prev,
+                          float *lookahead, int64_t rows, int64_t cols, const float *scalars,
+                          int32_t lookahead_merge, float lookahead_alpha, void *stream);
+
 /* Number of Full_Threats inputs implied by the offset table (the reference
  * asserts 60720, feature_extraction.rs:826). */
 int nnue_threat_table_total(void);

@@ -50,6 +50,7 @@ _SIGNATURES = {
         _I32, [_P, _P, _I32, _I64, _I32, _P, _P, _I64, _I32, _I32, _P, _I32, _P, _P, _P, _P, _P]),
     "nnue_ft_halfka_export_quantize": (_I32, [_P, _P, _I32, _I32, ctypes.c_float, ctypes.c_float, _P, _P, _P]),
     "nnue_ft_quantize_i16": (_I32, [_P, _I64, ctypes.c_float, _P, _P]),
+    "nnue_ft_ranger22_step": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I32, ctypes.c_float, _P]),
     "nnue_ft_gather_probe": (_I32, [_P, _I64, _P, _I32, _I32, _P, _P]),
     "nnue_threat_table_total": (_I32, []),
     "nnue_generate_positions": (_I32, [_U64, _I64, _I64, _P, _P]),

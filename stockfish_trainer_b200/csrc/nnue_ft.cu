@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "ft_backward.cuh"
 #include "ft_forward.cuh"
+#include "ft_optim.cuh"
 #include "ft_quant.cuh"
 
 namespace nnue {
@@ -924,6 +925,53 @@ int nnue_ft_quantize_i16(const float* x, int64_t n, float scale, int16_t* q, voi
   count_launch();
   quantize_i16_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, scale, q);
   return check_launch("quantize_i16");
+}
+
+int nnue_ft_ranger22_step(float* param, const float* grad, float* variance_ma, float* gma_cur, const float* gma_prev,
+                          float* lookahead, int64_t rows, int64_t cols, const float* scalars, int32_t lookahead_merge,
+                          float lookahead_alpha, void* stream) {
+  if (rows < 0 || cols < 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "ranger22_step: negative sizes");
+  if (rows == 0 || cols == 0) return NNUE_OK;
+  if (!param || !grad || !variance_ma || !gma_cur || !gma_prev || !scalars || (lookahead_merge && !lookahead))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "ranger22_step: null pointer");
+  R22Params a{};
+  a.p = param;
+  a.g = grad;
+  a.v = variance_ma;
+  a.m = gma_cur;
+  a.mp = gma_prev;
+  a.la = lookahead_merge ? lookahead : param;
+  a.rows = rows;
+  a.cols = cols;
+  a.lr = scalars[0];
+  a.inv_sqrt_bc2 = scalars[1];
+  a.eps = scalars[2];
+  a.two_nl = scalars[3];
+  a.noise_recip = scalars[4];
+  a.pnm_a = scalars[5];
+  a.pnm_b = scalars[6];
+  a.step_size = scalars[7];
+  a.beta2 = scalars[8];
+  a.omb2 = scalars[9];
+  a.b1sq = scalars[10];
+  a.omb1sq = scalars[11];
+  a.merge = lookahead_merge ? 1 : 0;
+  a.w = 1.0f - lookahead_alpha;
+  const bool v4 = cols % 4 == 0 && aligned16(param) && aligned16(grad) && aligned16(variance_ma) &&
+                  aligned16(gma_cur) && aligned16(gma_prev) && (!lookahead_merge || aligned16(lookahead));
+  const int64_t nvec = v4 ? cols / 4 : cols;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  count_launch();
+  if (nvec <= 32 * 64) {  // one warp per row, 8 rows per block
+    const unsigned grid = (unsigned)ceil_div(rows, 8);
+    if (v4) ranger22_rows_kernel<float4, 32><<<grid, 256, 0, s>>>(a);
+    else ranger22_rows_kernel<float, 32><<<grid, 256, 0, s>>>(a);
+  } else {  // one block per row
+    if (rows > INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "ranger22_step: too many long rows");
+    if (v4) ranger22_rows_kernel<float4, 512><<<(unsigned)rows, 512, 0, s>>>(a);
+    else ranger22_rows_kernel<float, 512><<<(unsigned)rows, 512, 0, s>>>(a);
+  }
+  return check_launch("ranger22_step");
 }
 
 size_t nnue_ft_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }

@@ -15,6 +15,7 @@ Fixtures and the reference code that produced them:
   quantize_ft.npz             src/model/quantize.py:76-93 (quantize_feature_transformer)
   export_weights.npz          src/model/modules/features/halfka_v2_hm.py:100-134 (get_export_weights)
   composed_sizes.npz          src/model/modules/features/composed.py:24-26, full_threats.py, halfka_v2_hm.py
+  ranger22_steps.npz          src/ranger22/optimizer.py (Ranger22.step, configured as src/train/common.py:155-169)
 """
 
 from __future__ import annotations
@@ -139,8 +140,44 @@ def main(ref_root: str) -> None:
         halfka_inputs=np.int64(halfka_v2_hm.HalfKav2Hm.NUM_INPUTS),
         threat_inputs=np.int64(full_threats.FullThreats.NUM_INPUTS),
     )
+    ranger22_fixture(ref_root)
     print("fixtures written to", HERE)
 
 
+def ranger22_fixture(ref_root: str) -> None:
+    """Seven Ranger22 steps (one lookahead merge at step 5) on a 2-D and a 1-D
+    CPU parameter with the trainer's configuration; CPU tensors take the
+    reference's baseline-equivalent path (optimizer.py:606-659)."""
+    if ref_root not in sys.path:
+        sys.path.insert(0, ref_root)
+    from src.ranger22 import Ranger22
+
+    gen = torch.Generator().manual_seed(22)
+    w = torch.nn.Parameter(torch.randn(6, 20, generator=gen) * 0.1)
+    b = torch.nn.Parameter(torch.randn(20, generator=gen) * 0.1)
+    w0, b0 = w.detach().clone(), b.detach().clone()
+    opt = Ranger22([{"params": [w, b]}], lr=8.75e-4, betas=(0.9, 0.999), eps=1.0e-7, using_gc=False,
+                   using_normgc=False, weight_decay=0.0, num_batches_per_epoch=100, num_epochs=10,
+                   warmdown_active=False, use_warmup=False, use_adaptive_gradient_clipping=False, softplus=False,
+                   pnm_momentum_factor=0.0)
+    steps = 7
+    gw = torch.randn(steps, 6, 20, generator=gen)
+    gb = torch.randn(steps, 20, generator=gen)
+    for s in range(steps):
+        w.grad = gw[s].clone()
+        b.grad = gb[s].clone()
+        opt.step()
+    out = {"w0": w0.numpy(), "b0": b0.numpy(), "gw": gw.numpy(), "gb": gb.numpy(), "lr": np.float64(8.75e-4),
+           "w": w.detach().numpy(), "b": b.detach().numpy()}
+    for name, p in (("w", w), ("b", b)):
+        st = opt.state[p]
+        for key in ("grad_ma", "neg_grad_ma", "variance_ma", "lookahead_params"):
+            out[f"{name}_{key}"] = st[key].numpy()
+    np.savez_compressed(os.path.join(HERE, "ranger22_steps.npz"), **out)
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) > 2 and sys.argv[2] == "ranger22":
+        ranger22_fixture(sys.argv[1])
+    else:
+        main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -54,7 +54,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe", "ranger22"],
+    p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe", "ranger22", "epilogue"],
                    default="headline",
                    help="headline: BASELINE configs[2]/[3] (the driver's metric); halfka: configs[1] "
                         "(HalfKAv2_hm^, B=16384, phases reported separately); quantized: configs[4] "
@@ -643,6 +643,81 @@ def run_ranger22(args):
     return 0
 
 
+def run_epilogue(args):
+    """FT epilogue: NNUEModel._transform_inputs after the
+    FT (model.py:93-115), forward + backward of both perspectives at the
+    headline batch, one fused kernel each way."""
+    import torch
+
+    from stockfish_trainer_b200 import _native
+    from stockfish_trainer_b200.feature_transformer import transform_inputs
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B = args.batch
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    wp = (torch.randn(B, C, device=dev, generator=gen) * 0.8 + 0.4).requires_grad_()
+    bp = (torch.randn(B, C, device=dev, generator=gen) * 0.8 + 0.4).requires_grad_()
+    us = (torch.rand(B, 1, device=dev, generator=gen) < 0.5).float()
+    pidx = torch.randint(0, NPSQT, (B,), device=dev, generator=gen)
+    d_l0 = torch.randn(B, L1, device=dev, generator=gen)
+    d_psqt = torch.randn(B, 1, device=dev, generator=gen)
+
+    def step():
+        l0, psqt = transform_inputs(wp, bp, us, pidx, L1)
+        torch.autograd.backward([l0, psqt], [d_l0, d_psqt])
+        wp.grad = None
+        bp.grad = None
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    l0c = _native.launch_count()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(e) / args.steps
+    launches = _native.launch_count() - l0c
+    row = C * 4
+    # forward: read wp, bp, us, index; write l0, psqt.  backward: read d_l0, d_psqt, wp, bp, us, index; write
+    # d_wp, d_bp
+    a_bytes = B * (2 * row + 4 + 8 + L1 * 4 + 4) + B * (L1 * 4 + 4 + 2 * row + 4 + 8 + 2 * row)
+    peak, src = hbm_peak()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import epilogue as oracle_epi
+
+        n = 4096
+        wc, bc = wp.detach()[:n].cpu(), bp.detach()[:n].cpu()
+        uc, pc, gl, gp = us[:n].cpu(), pidx[:n].cpu(), d_l0[:n].cpu(), d_psqt[:n].cpu()
+        oracle_epi.forward_backward(wc, bc, uc, pc, L1, gl, gp)
+        t0 = time.perf_counter()
+        reps = 5
+        for _ in range(reps):
+            oracle_epi.forward_backward(wc, bc, uc, pc, L1, gl, gp)
+        cpu_ms = (time.perf_counter() - t0) / reps * 1e3
+        cpu = {"value": n / (cpu_ms / 1e3), "unit": "positions/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"{n} positions, PyTorch CPU restatement of model.py:93-115 + autograd"}
+    emit({
+        "metric": "positions/s FT epilogue fwd+bwd (model.py _transform_inputs) @B=65536 L1=1040",
+        "value": B / (ms / 1e3), "unit": "positions/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic: FT outputs ~N(0.4, 0.8), random us / PSQT buckets",
+        "config": {"workload": "FT epilogue forward + backward, both perspectives", "batch": B, "L1": L1,
+                   "psqt": NPSQT, "l2": "inputs larger than L2, no flush"},
+        "roofline": {"bound": "hbm", "achieved": a_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": a_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
+                     "kernel": "ft_epilogue_forward_kernel + ft_epilogue_backward_kernel",
+                     "algorithmic_bytes": a_bytes, "peak_source": f"{src} hbm_gbs"},
+        "cpu_baseline": cpu,
+        "gpu_launches": int(launches),
+    })
+    return 0
+
+
 _JSON_FD = None
 
 
@@ -668,6 +743,8 @@ def main():
         return run_reference(args)
     if args.workload == "ranger22":
         return run_ranger22(args)
+    if args.workload == "epilogue":
+        return run_epilogue(args)
     if args.workload == "quantized":
         return run_quantized(args)
     if args.workload == "gather-probe":

@@ -44,6 +44,7 @@ extern "C" {
 #define NNUE_DEVERR_BAD_INDEX 1u         /* index < -1 or >= num_inputs was skipped */
 #define NNUE_DEVERR_BAD_QUANT_INDEX 2u   /* quantised forward: index outside the table */
 #define NNUE_DEVERR_BAD_SEGMENT 4u       /* backward: corrupt workspace (position out of range) */
+#define NNUE_DEVERR_BAD_PSQT_INDEX 8u    /* epilogue: PSQT bucket index outside [0, n_psqt) was skipped */
 
 /* ABI version (major * 100 + minor). */
 int nnue_ft_version(void);
@@ -195,6 +196,26 @@ int nnue_ft_halfka_export_quantize(const float *weight, const float *virtual_wei
 /* Elementwise fp32 -> int16 quantisation, round half to even (bias path of
  * quantize.py:83). */
 int nnue_ft_quantize_i16(const float *x, int64_t n, float scale, int16_t *q, void *stream);
+
+/* ---- FT epilogue (input transform) ---------------------------------------
+ * Replaces the tensor ops of NNUEModel._transform_inputs that follow the FT
+ * (src/model/model.py:93-115): split off the PSQT columns, clamp to [0, 1],
+ * pairwise product of the two halves, perspective order by `us`, x 127/128,
+ * PSQT bucket gather and (w - b) * (us - 0.5).  wp, bp: the FT outputs
+ * [batch, l1 + n_psqt] fp32; us: [batch] fp32 (0 or 1; the reference's
+ * [batch, 1] tensor); psqt_indices: [batch] int64.  l1 must be even.
+ * Forward writes l0 [batch, l1] and psqt [batch]. */
+int nnue_ft_epilogue_forward(const float *wp, const float *bp, int64_t batch, int32_t l1, int32_t n_psqt,
+                             const float *us, const int64_t *psqt_indices, float *l0, float *psqt, void *stream);
+
+/* Backward of the same graph: the gradients torch autograd produces for it,
+ * bit for bit (clamp passes gradient only inside [0, 1], the where / select /
+ * gather backward terms are added in autograd's way).  grad_l0 and grad_psqt
+ * may be null (zero gradient).  Writes grad_wp and grad_bp [batch, l1 + n_psqt]
+ * completely: they are the FT backward's grad_output. */
+int nnue_ft_epilogue_backward(const float *wp, const float *bp, int64_t batch, int32_t l1, int32_t n_psqt,
+                              const float *us, const int64_t *psqt_indices, const float *grad_l0,
+                              const float *grad_psqt, float *grad_wp, float *grad_bp, void *stream);
 
 /* ---- Ranger22 parameter update ------------------------------------------
  * Replaces, for one fp32 parameter, the update of Ranger22.step's fused path

@@ -27,6 +27,7 @@ NNUE_ERR_WORKSPACE = -3
 NNUE_ERR_CUDA = -4
 DEVERR_BAD_INDEX = 1
 DEVERR_BAD_QUANT_INDEX = 2
+DEVERR_BAD_PSQT_INDEX = 8
 
 _SIGNATURES = {
     "nnue_ft_version": (_I32, []),
@@ -51,6 +52,8 @@ _SIGNATURES = {
     "nnue_ft_halfka_export_quantize": (_I32, [_P, _P, _I32, _I32, ctypes.c_float, ctypes.c_float, _P, _P, _P]),
     "nnue_ft_quantize_i16": (_I32, [_P, _I64, ctypes.c_float, _P, _P]),
     "nnue_ft_ranger22_step": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I32, ctypes.c_float, _P]),
+    "nnue_ft_epilogue_forward": (_I32, [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P]),
+    "nnue_ft_epilogue_backward": (_I32, [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "nnue_ft_gather_probe": (_I32, [_P, _I64, _P, _I32, _I32, _P, _P]),
     "nnue_threat_table_total": (_I32, []),
     "nnue_generate_positions": (_I32, [_U64, _I64, _I64, _P, _P]),

@@ -20,6 +20,7 @@ enum : unsigned {
   kErrBadIndex = 1u,       // feature index < -1 or >= num_inputs
   kErrBadQuantIndex = 2u,  // quantised forward: index outside the table / export map
   kErrBadSegment = 4u,     // backward: a sorted position outside [0, batch) (corrupt workspace)
+  kErrBadPsqtIndex = 8u,   // epilogue: PSQT bucket index outside [0, n_psqt)
 };
 
 __device__ __forceinline__ void flag_error(unsigned e) { atomicOr(&g_device_errors, e); }

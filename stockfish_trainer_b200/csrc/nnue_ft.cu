@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "ft_backward.cuh"
 #include "ft_forward.cuh"
+#include "ft_epilogue.cuh"
 #include "ft_optim.cuh"
 #include "ft_quant.cuh"
 
@@ -925,6 +926,59 @@ int nnue_ft_quantize_i16(const float* x, int64_t n, float scale, int16_t* q, voi
   count_launch();
   quantize_i16_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, scale, q);
   return check_launch("quantize_i16");
+}
+
+namespace {
+int epilogue_launch(bool backward, const float* wp, const float* bp, int64_t batch, int32_t l1, int32_t n_psqt,
+                    const float* us, const int64_t* pidx, float* l0, float* psqt, const float* g_l0,
+                    const float* g_psqt, float* g_wp, float* g_bp, void* stream) {
+  const char* what = backward ? "epilogue_backward" : "epilogue_forward";
+  if (batch < 0 || l1 <= 0 || l1 % 2 != 0 || n_psqt < 0)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "%s: need batch >= 0, even l1 > 0, n_psqt >= 0", what);
+  if (batch == 0) return NNUE_OK;
+  if (!wp || !bp || !us || !pidx || (!backward && (!l0 || !psqt)) || (backward && (!g_wp || !g_bp)))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  EpiParams a{};
+  a.wp = wp;
+  a.bp = bp;
+  a.us = us;
+  a.pidx = pidx;
+  a.l0 = l0;
+  a.psqt = psqt;
+  a.d_l0 = g_l0;
+  a.d_psqt = g_psqt;
+  a.d_wp = g_wp;
+  a.d_bp = g_bp;
+  a.B = batch;
+  a.l1 = l1;
+  a.n_psqt = n_psqt;
+  const bool v4 = l1 % 8 == 0 && (l1 + n_psqt) % 4 == 0 && aligned16(wp) && aligned16(bp) &&
+                  (backward ? (aligned16(g_wp) && aligned16(g_bp) && (!g_l0 || aligned16(g_l0))) : aligned16(l0));
+  const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(batch, 8), 148 * 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  count_launch();
+  if (backward) {
+    if (v4) ft_epilogue_backward_kernel<float4><<<grid, 256, 0, s>>>(a);
+    else ft_epilogue_backward_kernel<float><<<grid, 256, 0, s>>>(a);
+  } else {
+    if (v4) ft_epilogue_forward_kernel<float4><<<grid, 256, 0, s>>>(a);
+    else ft_epilogue_forward_kernel<float><<<grid, 256, 0, s>>>(a);
+  }
+  return check_launch(what);
+}
+}  // namespace
+
+int nnue_ft_epilogue_forward(const float* wp, const float* bp, int64_t batch, int32_t l1, int32_t n_psqt,
+                             const float* us, const int64_t* psqt_indices, float* l0, float* psqt, void* stream) {
+  return epilogue_launch(false, wp, bp, batch, l1, n_psqt, us, psqt_indices, l0, psqt, nullptr, nullptr, nullptr,
+                         nullptr, stream);
+}
+
+int nnue_ft_epilogue_backward(const float* wp, const float* bp, int64_t batch, int32_t l1, int32_t n_psqt,
+                              const float* us, const int64_t* psqt_indices, const float* grad_l0,
+                              const float* grad_psqt, float* grad_wp, float* grad_bp, void* stream) {
+  return epilogue_launch(true, wp, bp, batch, l1, n_psqt, us, psqt_indices, nullptr, nullptr, grad_l0, grad_psqt,
+                         grad_wp, grad_bp, stream);
 }
 
 int nnue_ft_ranger22_step(float* param, const float* grad, float* variance_ma, float* gma_cur, const float* gma_prev,

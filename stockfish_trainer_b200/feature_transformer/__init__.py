@@ -1,9 +1,12 @@
 """Drop-in for src/model/modules/feature_transformer (reference __init__.py:1-5)."""
 
+from .epilogue import TransformInputsFunction, transform_inputs
 from .functions import SparseLinearFunction, SparseLinearPairFunction
 from .kernel import make_sparse_input_linear_backward_kernel, make_sparse_input_linear_forward_kernel
 
 __all__ = [
+    "TransformInputsFunction",
+    "transform_inputs",
     "SparseLinearFunction",
     "SparseLinearPairFunction",
     "make_sparse_input_linear_forward_kernel",

@@ -16,6 +16,7 @@ Fixtures and the reference code that produced them:
   export_weights.npz          src/model/modules/features/halfka_v2_hm.py:100-134 (get_export_weights)
   composed_sizes.npz          src/model/modules/features/composed.py:24-26, full_threats.py, halfka_v2_hm.py
   ranger22_steps.npz          src/ranger22/optimizer.py (Ranger22.step, configured as src/train/common.py:155-169)
+  transform_inputs.npz        src/model/model.py:86-115 (NNUEModel._transform_inputs, forward + autograd backward)
 """
 
 from __future__ import annotations
@@ -141,7 +142,45 @@ def main(ref_root: str) -> None:
         threat_inputs=np.int64(full_threats.FullThreats.NUM_INPUTS),
     )
     ranger22_fixture(ref_root)
+    transform_inputs_fixture(ref_root)
     print("fixtures written to", HERE)
+
+
+def transform_inputs_fixture(ref_root: str) -> None:
+    """NNUEModel._transform_inputs on given FT outputs (the FT call is stubbed
+    to return them), forward and autograd backward, small L1."""
+    if "chess" not in sys.modules:
+        _install_chess_stub()
+    if ref_root not in sys.path:
+        sys.path.insert(0, ref_root)
+    from src.model.model import NNUEModel
+
+    B, L1, NP = 40, 24, 8
+    gen = torch.Generator().manual_seed(7)
+    wp = torch.randn(B, L1 + NP, generator=gen) * 0.8 + 0.4
+    bp = torch.randn(B, L1 + NP, generator=gen) * 0.8 + 0.4
+    wp[0, :6] = torch.tensor([0.0, 1.0, -0.0, 1.5, -0.25, 0.5])  # clamp edges
+    bp[1, :6] = torch.tensor([1.0, 0.0, 2.0, -0.0, 0.999, 1e-30])
+    us = (torch.rand(B, 1, generator=gen) < 0.5).float()
+    pidx = torch.randint(0, NP, (B,), generator=gen)
+    d_l0 = torch.randn(B, L1, generator=gen)
+    d_l0[2, :4] = torch.tensor([-0.0, 0.0, -1.0, 1.0])
+    d_psqt = torch.randn(B, 1, generator=gen)
+    d_psqt[3, 0] = -0.0
+
+    class _Stub:
+        pass
+
+    stub = _Stub()
+    stub.L1 = L1
+    wpg, bpg = wp.clone().requires_grad_(), bp.clone().requires_grad_()
+    stub.input = lambda wi, bi: (wpg, bpg)
+    l0, psqt = NNUEModel._transform_inputs(stub, us, None, None, pidx)
+    torch.autograd.backward([l0, psqt], [d_l0, d_psqt])
+    np.savez_compressed(os.path.join(HERE, "transform_inputs.npz"), wp=wp.numpy(), bp=bp.numpy(), us=us.numpy(),
+                        psqt_indices=pidx.numpy(), d_l0=d_l0.numpy(), d_psqt=d_psqt.numpy(),
+                        l0=l0.detach().numpy(), psqt=psqt.detach().numpy(), d_wp=wpg.grad.numpy(),
+                        d_bp=bpg.grad.numpy(), l1=np.int64(L1))
 
 
 def ranger22_fixture(ref_root: str) -> None:
@@ -179,5 +218,7 @@ def ranger22_fixture(ref_root: str) -> None:
 if __name__ == "__main__":
     if len(sys.argv) > 2 and sys.argv[2] == "ranger22":
         ranger22_fixture(sys.argv[1])
+    elif len(sys.argv) > 2 and sys.argv[2] == "transform_inputs":
+        transform_inputs_fixture(sys.argv[1])
     else:
         main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -54,7 +54,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe", "ranger22", "epilogue"],
+    p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe", "ranger22", "epilogue",
+                                          "composed"],
                    default="headline",
                    help="headline: BASELINE configs[2]/[3] (the driver's metric); halfka: configs[1] "
                         "(HalfKAv2_hm^, B=16384, phases reported separately); quantized: configs[4] "
@@ -718,6 +719,100 @@ def run_epilogue(args):
     return 0
 
 
+def run_composed(args):
+    """Module-level composed FT: ComposedFeatureTransformer
+    forward + backward through autograd at the headline size, the per-feature
+    tables read in place (no merged copy), against the reference module's
+    graph (torch.cat of the per-feature tables with the virtual rows repeated,
+    then the FT op) run with this library's FT op on the same GPU."""
+    import torch
+    from torch import nn
+
+    from stockfish_trainer_b200 import _native, positions
+    from stockfish_trainer_b200.feature_transformer import SparseLinearPairFunction
+    from stockfish_trainer_b200.feature_transformer.composed import ComposedFeatureTransformer
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B = args.batch
+    white, black, _ = positions.synthetic_batch(B, "Full_Threats+HalfKAv2_hm^", seed=args.seed)
+
+    class Feature(nn.Module):
+        def __init__(self, rows, virtual_rows, name, h, max_active, real):
+            super().__init__()
+            self.num_outputs, self.NUM_INPUTS, self.FEATURE_NAME = C, rows, name
+            self.INPUT_FEATURE_NAME, self.HASH, self.MAX_ACTIVE_FEATURES, self.NUM_REAL_FEATURES = name, h, max_active, real
+            self.weight = nn.Parameter(torch.randn(rows, C, device=dev) * 0.01)
+            if virtual_rows:
+                self.NUM_BUCKETS = rows // virtual_rows
+                self.virtual_weight = nn.Parameter(torch.randn(virtual_rows, C, device=dev) * 0.001)
+
+        def merged_weight(self):
+            if hasattr(self, "virtual_weight"):
+                return self.weight + self.virtual_weight.repeat(self.NUM_BUCKETS, 1)
+            return self.weight
+
+    torch.manual_seed(args.seed)
+    feats = [Feature(60720, 0, "Full_Threats", 0x8F234CB8, 128, 60720),
+             Feature(24576, 768, "HalfKAv2_hm^", 0x7F234CB8, 32, 22528)]
+    module = ComposedFeatureTransformer(feats).to(dev)
+    i0, i1 = torch.from_numpy(white).to(dev), torch.from_numpy(black).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    d0 = torch.randn(B, C, device=dev, generator=gen)
+    d1 = torch.randn(B, C, device=dev, generator=gen)
+
+    def fused():
+        o0, o1 = module(i0, i1)
+        torch.autograd.backward([o0, o1], [d0, d1])
+        for p in module.parameters():
+            p.grad = None
+
+    def cat_path():
+        merged = torch.cat([f.merged_weight() for f in feats], dim=0)
+        o0, o1 = SparseLinearPairFunction.apply(i0, i1, merged, module.bias)
+        torch.autograd.backward([o0, o1], [d0, d1])
+        for p in module.parameters():
+            p.grad = None
+
+    def timeit(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(e) / args.steps
+
+    ms_cat = timeit(cat_path)
+    l0c = _native.launch_count()
+    ms = timeit(fused)
+    launches = _native.launch_count() - l0c
+    nnz = int((white >= 0).sum() + (black >= 0).sum())
+    T, K = 85296, white.shape[1]
+    a_bytes = (nnz * C * 4 + 2 * B * C * 4 + 2 * B * K * 4) + (nnz * C * 4 + 2 * B * K * 4 + T * C * 4)
+    peak, src = hbm_peak()
+    emit({
+        "metric": "positions/s composed FT module fwd+bwd (Full_Threats+HalfKAv2_hm^, autograd) @B=65536 L1=1040",
+        "value": B / (ms / 1e3), "unit": "positions/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": DATA,
+        "config": {"workload": "ComposedFeatureTransformer forward + backward (threat table, HalfKA table + 768 "
+                               "virtual rows, bias) through autograd", "batch": B, "L1": L1, "psqt": NPSQT,
+                   "l2": "inputs larger than L2, no flush"},
+        "roofline": {"bound": "hbm", "achieved": a_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": a_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
+                     "kernel": "module step (SURVEY 8(d) A_step)", "algorithmic_bytes": a_bytes,
+                     "peak_source": f"{src} hbm_gbs"},
+        "cat_path_same_gpu": {"ms_per_step": ms_cat, "value": B / (ms_cat / 1e3), "unit": "positions/s",
+                              "what": "reference module graph (torch.cat + repeat) with this library's FT op"},
+        "gpu_launches": int(launches),
+    })
+    return 0
+
+
 _JSON_FD = None
 
 
@@ -745,6 +840,8 @@ def main():
         return run_ranger22(args)
     if args.workload == "epilogue":
         return run_epilogue(args)
+    if args.workload == "composed":
+        return run_composed(args)
     if args.workload == "quantized":
         return run_quantized(args)
     if args.workload == "gather-probe":

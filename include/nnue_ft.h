@@ -197,6 +197,42 @@ int nnue_ft_halfka_export_quantize(const float *weight, const float *virtual_wei
  * quantize.py:83). */
 int nnue_ft_quantize_i16(const float *x, int64_t n, float scale, int16_t *q, void *stream);
 
+/* ---- composed feature sets: tables in separate allocations ---------------
+ * Replaces ComposedFeatureTransformer.forward's
+ *   merged = torch.cat([f.merged_weight() for f in self.features], dim=0)
+ * (src/model/modules/features/composed.py:49-54) followed by the two
+ * SparseLinearFunction calls, and the backward's split of the merged
+ * gradient into the per-feature parameters: global row f of the feature set
+ * lives in table t (the first with f < rows[0] + ... + rows[t]) at local row
+ * f - (rows[0] + ... + rows[t-1]).  tables / weight_grads are HOST arrays of
+ * n_tables (1..4) device pointers, each [rows[t], output_size] fp32.
+ * Results equal the merged-table calls bit for bit; no merged copy is made. */
+int nnue_ft_forward_pair_tables(const int32_t *idx0, const int32_t *idx1, int64_t batch, int32_t max_active,
+                                const float *const *tables, const int64_t *table_rows, int32_t n_tables,
+                                int32_t output_size, const float *bias, float *out0, float *out1, void *stream);
+
+/* The same forward with the backward's index phase on the library's side
+ * stream (like nnue_ft_forward_pair_prepare; num_inputs = sum of rows). */
+int nnue_ft_forward_pair_tables_prepare(const int32_t *idx0, const int32_t *idx1, int64_t batch, int32_t max_active,
+                                        const float *const *tables, const int64_t *table_rows, int32_t n_tables,
+                                        int32_t output_size, const float *bias, float *out0, float *out1,
+                                        void *workspace, size_t workspace_bytes, void *stream);
+
+/* nnue_ft_backward_apply for two perspectives with weight_grads split like
+ * the tables: every row of every weight_grads[t] is written (or accumulated
+ * into when accumulate != 0, touched rows only). */
+int nnue_ft_backward_apply_tables(const float *grad0, const float *grad1, int64_t batch, int32_t max_active,
+                                  float *const *weight_grads, const int64_t *table_rows, int32_t n_tables,
+                                  int32_t output_size, float *bias_grad, int32_t accumulate, void *workspace,
+                                  size_t workspace_bytes, void *stream);
+
+/* HalfKav2Hm.merged_weight (halfka_v2_hm.py:69-70):
+ * out[r] = weight[r] + virtual_weight[r % period] for r < rows (rows a
+ * multiple of period), one fp32 add per element, without materialising
+ * virtual_weight.repeat(rows / period, 1). */
+int nnue_ft_merge_virtual(const float *weight, int64_t rows, const float *virtual_weight, int64_t period,
+                          int32_t cols, float *out, void *stream);
+
 /* ---- FT epilogue (input transform) ---------------------------------------
  * Replaces the tensor ops of NNUEModel._transform_inputs that follow the FT
  * (src/model/model.py:93-115): split off the PSQT columns, clamp to [0, 1],

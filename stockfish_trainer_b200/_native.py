@@ -53,6 +53,11 @@ _SIGNATURES = {
     "nnue_ft_quantize_i16": (_I32, [_P, _I64, ctypes.c_float, _P, _P]),
     "nnue_ft_ranger22_step": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I32, ctypes.c_float, _P]),
     "nnue_ft_epilogue_forward": (_I32, [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P]),
+    "nnue_ft_forward_pair_tables": (_I32, [_P, _P, _I64, _I32, _P, _P, _I32, _I32, _P, _P, _P, _P]),
+    "nnue_ft_forward_pair_tables_prepare": (_I32, [_P, _P, _I64, _I32, _P, _P, _I32, _I32, _P, _P, _P, _P, _SZ,
+                                                    _P]),
+    "nnue_ft_backward_apply_tables": (_I32, [_P, _P, _I64, _I32, _P, _P, _I32, _I32, _P, _I32, _P, _SZ, _P]),
+    "nnue_ft_merge_virtual": (_I32, [_P, _I64, _P, _I64, _I32, _P, _P]),
     "nnue_ft_epilogue_backward": (_I32, [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "nnue_ft_gather_probe": (_I32, [_P, _I64, _P, _I32, _I32, _P, _P]),
     "nnue_threat_table_total": (_I32, []),

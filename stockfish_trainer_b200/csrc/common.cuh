@@ -59,6 +59,25 @@ struct Vec<float> {
   static __device__ __forceinline__ void st_stream(float* p, const float& v) { __stcs(p, v); }
 };
 
+// A feature table split over up to kMaxTables separately allocated row
+// blocks (the reference's per-feature parameters, composed.py:49-50): global
+// row f lives in block t = the first with f < end[t], at local row
+// f - end[t - 1].  n == 1 means one contiguous table (the fast path).
+constexpr int kMaxTables = 4;
+struct TableSet {
+  float* base[kMaxTables];
+  int32_t end[kMaxTables];
+  int32_t n;
+  __host__ __device__ __forceinline__ int find(int64_t f) const {
+    int t = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxTables - 1; ++i)
+      if (i < n - 1 && f >= end[i]) t = i + 1;
+    return t;
+  }
+  __host__ __device__ __forceinline__ int64_t start(int t) const { return t ? end[t - 1] : 0; }
+};
+
 // Column chunking of one table row of n_vec vectors into n_chunks balanced
 // chunks: chunk c covers vectors [begin(c), begin(c + 1)), widths differ by
 // at most one.  Chunks are the OUTER grid dimension, so at any moment the

@@ -629,6 +629,7 @@ struct SegParams {
   int32_t row_begin;          // rows [row_begin, row_end) of dW are produced by this call
   int32_t row_end;
   Geom g;
+  TableSet dws;               // n > 1: dW split over separately allocated row blocks (dW unused)
 };
 
 // Decodes a sorted value of perspective q; out-of-range values (a corrupt
@@ -646,7 +647,13 @@ template <typename VT, int V>
 __device__ __forceinline__ void seg_write(const SegParams& p, int64_t f, int col, const VT (&tot)[V],
                                           const bool (&ok)[V], bool touched) {
   using Ops = Vec<VT>;
-  VT* dst = reinterpret_cast<VT*>(p.dW) + f * (int64_t)p.g.n_vec + col;
+  VT* dst;
+  if (p.dws.n > 1) {
+    const int t = p.dws.find(f);
+    dst = reinterpret_cast<VT*>(p.dws.base[t]) + (f - p.dws.start(t)) * (int64_t)p.g.n_vec + col;
+  } else {
+    dst = reinterpret_cast<VT*>(p.dW) + f * (int64_t)p.g.n_vec + col;
+  }
   if (p.accumulate) {
     if (!touched) return;
 #pragma unroll

@@ -14,6 +14,8 @@
 // column vectors, which keeps the per-column add order.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace nnue {
@@ -30,6 +32,7 @@ struct FwdParams {
   int32_t items_per_warp;  // consecutive (perspective, position) items per warp
   int32_t chunk0;          // first column chunk of this launch (blockIdx.y offset)
   Geom g;
+  TableSet tabs;           // MULTI kernels: W split over separately allocated row blocks
 };
 
 constexpr int kIdxGroups = 8;  // index slots read per item in one go: 8 x 32 = 256
@@ -62,6 +65,29 @@ __device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, 
   return n;
 }
 
+// Table-set form of compact_valid: the list holds each valid row's address
+// in its own block (lane-independent: block base + local row + chunk start).
+template <typename VT>
+__device__ __forceinline__ int compact_rows(const int (&f)[kIdxGroups], int T, const TableSet& tabs, int row_vec,
+                                            int c0, const VT** list, int lane) {
+  const unsigned lt = lanemask_lt();
+  int n = 0;
+#pragma unroll
+  for (int g = 0; g < kIdxGroups; ++g) {
+    const bool valid = (unsigned)f[g] < (unsigned)T;
+    if (!valid && f[g] != -1) flag_error(kErrBadIndex);
+    const unsigned m = __ballot_sync(kFull, valid);
+    if (valid) {
+      const int t = tabs.find(f[g]);
+      list[n + __popc(m & lt)] =
+          reinterpret_cast<const VT*>(tabs.base[t]) + (f[g] - tabs.start(t)) * (int64_t)row_vec + c0;
+    }
+    n += __popc(m);
+  }
+  __syncwarp();
+  return n;
+}
+
 // The rows of an item stream through a D-slot register queue: consuming
 // slot d immediately re-issues it with the row D further on, so D rows stay
 // in flight for the whole item.  The compacted list holds row OFFSETS (index
@@ -69,12 +95,14 @@ __device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, 
 // kernel is latency-bound: bytes in flight per SM are resident warps x D x
 // one row slice, so MINB (resident blocks the register budget is sized for)
 // matters as much as D.
-template <typename VT, int V, int D, int MINB = 1>
+template <typename VT, int V, int D, int MINB = 1, bool MULTI = false>
 __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParams p) {
   using Ops = Vec<VT>;
-  __shared__ int s_list[kWarpsPerBlock][32 * kIdxGroups];
+  // one table: 32-bit row offsets; table set: row addresses
+  using Entry = std::conditional_t<MULTI, const VT*, int>;
+  __shared__ Entry s_list[kWarpsPerBlock][32 * kIdxGroups];
   const int lane = threadIdx.x & 31;
-  int* list = s_list[threadIdx.x >> 5];
+  Entry* list = s_list[threadIdx.x >> 5];
   const int chunk = p.chunk0 + blockIdx.y;
   const int c0 = p.g.begin(chunk);
   const int width = p.g.width(chunk);
@@ -106,15 +134,23 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
     for (int v = 0; v < V; ++v) acc[v] = ok[v] ? Ops::ldg(bvec + 32 * v) : Ops::zero();
     for (int sg = 0; sg < n_super; ++sg) {
       if (sg > 0) load_index_groups(irow, p.K, sg * kIdxGroups, lane, f);
-      const int n = compact_valid(f, p.T, list, lane, row_vec);
+      int n;
+      if constexpr (MULTI) n = compact_rows<VT>(f, p.T, p.tabs, row_vec, c0, list, lane);
+      else n = compact_valid(f, p.T, list, lane, row_vec);
       // the next item's indices load while this item's rows are in flight
       if (sg == n_super - 1 && item + 1 < item_end) load_index_groups(index_row(item + 1), p.K, 0, lane, f);
       VT w[D][V];
+      auto row_ptr = [&](const Entry e) -> const VT* {
+        if constexpr (MULTI) return e + lane;
+        else return Wv + e;
+      };
       auto issue = [&](int slot, int j) {
-        const int off = j < n ? list[j] : -1;
+        if (j < n) {
+          const VT* a = row_ptr(list[j]);
 #pragma unroll
-        for (int v = 0; v < V; ++v)
-          if (off >= 0 && ok[v]) w[slot][v] = Ops::ldg(Wv + off + 32 * v);
+          for (int v = 0; v < V; ++v)
+            if (ok[v]) w[slot][v] = Ops::ldg(a + 32 * v);
+        }
       };
 #pragma unroll
       for (int d = 0; d < D; ++d) issue(d, d);
@@ -126,10 +162,10 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
 #pragma unroll
           for (int v = 0; v < V; ++v)
             if (ok[v]) Ops::add(acc[v], w[d][v]);
-          const int off = list[j0 + d + D];
+          const VT* a = row_ptr(list[j0 + d + D]);
 #pragma unroll
           for (int v = 0; v < V; ++v)
-            if (ok[v]) w[d][v] = Ops::ldg(Wv + off + 32 * v);
+            if (ok[v]) w[d][v] = Ops::ldg(a + 32 * v);
         }
       }
       for (; j0 < n; j0 += D) {
@@ -149,6 +185,22 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
 #pragma unroll
     for (int v = 0; v < V; ++v)
       if (ok[v]) Ops::st_stream(o + 32 * v, acc[v]);
+  }
+}
+
+// out[r] = weight[r] + virtual_weight[r % period], one fp32 add per element:
+// HalfKav2Hm.merged_weight (halfka_v2_hm.py:69-70, weight +
+// virtual_weight.repeat(NUM_BUCKETS, 1)) without materialising the repeat.
+template <typename VT>
+__global__ void __launch_bounds__(256) merge_virtual_kernel(const VT* __restrict__ w, const VT* __restrict__ vw,
+                                                            int64_t n, int64_t row_vec, int64_t period,
+                                                            VT* __restrict__ out) {
+  using Ops = Vec<VT>;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / row_vec, c = i - r * row_vec;
+    VT x = __ldcs(w + i);
+    Ops::add(x, __ldg(vw + (r % period) * row_vec + c));
+    out[i] = x;
   }
 }
 

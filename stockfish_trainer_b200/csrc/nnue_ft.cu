@@ -135,7 +135,8 @@ void launch_forward_vd(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(warps, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
-  ft_forward_kernel<VT, V, D, MINB><<<grid, kBlock, 0, s>>>(p);
+  if (p.tabs.n > 1) ft_forward_kernel<VT, V, D, MINB, true><<<grid, kBlock, 0, s>>>(p);
+  else ft_forward_kernel<VT, V, D, MINB, false><<<grid, kBlock, 0, s>>>(p);
 }
 
 template <typename VT, int V, int D>
@@ -177,15 +178,42 @@ void launch_forward(const FwdParams& p, cudaStream_t s) {
   launch_forward_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
 }
 
+// Builds a table set from per-block pointers and row counts (n_tables >= 1).
+int make_tables(const char* what, float* const* bases, const int64_t* rows, int32_t n_tables, TableSet& t,
+                int64_t& total) {
+  if (n_tables < 1 || n_tables > kMaxTables)
+    return fail(NNUE_ERR_UNSUPPORTED, "%s: 1..%d tables supported, got %d", what, kMaxTables, (int)n_tables);
+  if (!bases || !rows) return fail(NNUE_ERR_INVALID_ARGUMENT, "%s: null table list", what);
+  t = TableSet{};
+  t.n = n_tables;
+  total = 0;
+  for (int i = 0; i < n_tables; ++i) {
+    if (rows[i] < 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "%s: negative row count", what);
+    if (rows[i] > 0 && !bases[i]) return fail(NNUE_ERR_INVALID_ARGUMENT, "%s: null table %d", what, i);
+    total += rows[i];
+    if (total > INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "%s: tables exceed int32 index range", what);
+    t.base[i] = bases[i];
+    t.end[i] = (int32_t)total;
+  }
+  return NNUE_OK;
+}
+
+bool tables_aligned16(const TableSet& t) {
+  for (int i = 0; i < t.n; ++i)
+    if (!aligned16(t.base[i])) return false;
+  return true;
+}
+
 int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int32_t K, const float* W,
-                 int64_t T, int32_t C, const float* bias, float* out0, float* out1, cudaStream_t s) {
+                 int64_t T, int32_t C, const float* bias, float* out0, float* out1, cudaStream_t s,
+                 const TableSet* tabs = nullptr) {
   if (B < 0 || K < 0 || T < 0 || C <= 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "forward: bad sizes");
   if (T > INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "forward: num_inputs exceeds int32 index range");
   if (B == 0) return NNUE_OK;
-  if (!idx0 || !out0 || !bias || (T > 0 && !W) || (P == 2 && (!idx1 || !out1)))
+  if (!idx0 || !out0 || !bias || (T > 0 && !W && !tabs) || (P == 2 && (!idx1 || !out1)))
     return fail(NNUE_ERR_INVALID_ARGUMENT, "forward: null pointer");
-  const bool v4 = (C % 4 == 0) && aligned16(W) && aligned16(bias) && aligned16(out0) &&
-                  (P == 1 || aligned16(out1));
+  const bool v4 = (C % 4 == 0) && (tabs ? tables_aligned16(*tabs) : aligned16(W)) && aligned16(bias) &&
+                  aligned16(out0) && (P == 1 || aligned16(out1));
   FwdParams p{};
   p.idx[0] = idx0;
   p.idx[1] = P == 2 ? idx1 : idx0;
@@ -198,6 +226,9 @@ int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int
   p.T = (int32_t)T;
   p.P = P;
   p.items_per_warp = (int32_t)g_tune.fwd_items_per_warp;
+  if (tabs && tabs->n > 1) p.tabs = *tabs;
+  else p.tabs.n = 1;
+  if (tabs && tabs->n == 1) p.W = tabs->base[0];
   p.g = v4 ? make_geom(C / 4, g_tune.fwd_chunk_vec, g_tune.fwd_exact_chunks)
              : make_geom(C, g_tune.fwd_chunk_vec * 4, g_tune.fwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "forward: column chunk too wide");
@@ -558,13 +589,15 @@ int launch_segsum_stream(const SegParams& p, cudaStream_t s) {
 }
 
 int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w, float* dW, float* dB,
-               int32_t accumulate, int64_t row_begin, int64_t row_end, bool with_bias, cudaStream_t s) {
+               int32_t accumulate, int64_t row_begin, int64_t row_end, bool with_bias, cudaStream_t s,
+               const TableSet* dws = nullptr) {
   if (row_begin < 0 || row_end > pl.T || row_begin > row_end)
     return fail(NNUE_ERR_INVALID_ARGUMENT, "backward_apply: row range [%lld, %lld) outside [0, %lld)",
                 (long long)row_begin, (long long)row_end, (long long)pl.T);
   if (row_begin == row_end && !with_bias) return NNUE_OK;
-  const bool v4 = (pl.C % 4 == 0) && aligned16(g0) && (pl.P == 1 || aligned16(g1)) && aligned16(dW) &&
-                  (!with_bias || aligned16(dB)) && aligned16(w.partial);
+  const bool v4 = (pl.C % 4 == 0) && aligned16(g0) && (pl.P == 1 || aligned16(g1)) &&
+                  (dws ? tables_aligned16(*dws) : aligned16(dW)) && (!with_bias || aligned16(dB)) &&
+                  aligned16(w.partial);
   SegParams p{};
   p.dout[0] = g0;
   p.dout[1] = pl.P == 2 ? g1 : g0;
@@ -583,6 +616,9 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   p.n_stream_warps = (int32_t)pl.n_stream_warps;
   p.row_begin = (int32_t)row_begin;
   p.row_end = (int32_t)row_end;
+  if (dws && dws->n > 1) p.dws = *dws;
+  else p.dws.n = 1;
+  if (dws && dws->n == 1) p.dW = dws->base[0];
   p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec, g_tune.bwd_exact_chunks)
              : make_geom(pl.C, g_tune.bwd_chunk_vec * 4, g_tune.bwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "backward: column chunk too wide");
@@ -791,6 +827,90 @@ int nnue_ft_forward_pair_prepare(const int32_t* idx0, const int32_t* idx1, int64
   if (rc != NNUE_OK) return rc;
   if (cudaStreamWaitEvent(s, aux->join, 0) != cudaSuccess) return check_launch("forward_pair_prepare: join");
   return NNUE_OK;
+}
+
+int nnue_ft_forward_pair_tables(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active,
+                                const float* const* tables, const int64_t* table_rows, int32_t n_tables,
+                                int32_t output_size, const float* bias, float* out0, float* out1, void* stream) {
+  TableSet t;
+  int64_t T = 0;
+  int rc = make_tables("forward_pair_tables", const_cast<float* const*>(tables), table_rows, n_tables, t, T);
+  if (rc != NNUE_OK) return rc;
+  return forward_impl(idx0, idx1, 2, batch, max_active, nullptr, T, output_size, bias, out0, out1,
+                      static_cast<cudaStream_t>(stream), &t);
+}
+
+int nnue_ft_forward_pair_tables_prepare(const int32_t* idx0, const int32_t* idx1, int64_t batch, int32_t max_active,
+                                        const float* const* tables, const int64_t* table_rows, int32_t n_tables,
+                                        int32_t output_size, const float* bias, float* out0, float* out1,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  TableSet t;
+  int64_t T = 0;
+  int rc = make_tables("forward_pair_tables_prepare", const_cast<float* const*>(tables), table_rows, n_tables, t, T);
+  if (rc != NNUE_OK) return rc;
+  BwdPlan pl;
+  rc = make_plan(batch, max_active, T, output_size, 2, pl);
+  if (rc != NNUE_OK) return rc;
+  rc = check_bwd_args(idx0, idx1, 2, workspace, workspace_bytes, pl);
+  if (rc != NNUE_OK) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceAux* aux = nullptr;
+  rc = device_aux(&aux);
+  if (rc != NNUE_OK) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_aux_mu);
+    if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
+      return check_launch("forward_pair_tables_prepare: fork");
+    rc = prepare_impl(idx0, idx1, pl, carve(pl, workspace), aux->side);
+    if (rc != NNUE_OK) return rc;
+    if (cudaEventRecord(aux->join, aux->side) != cudaSuccess)
+      return check_launch("forward_pair_tables_prepare: join record");
+  }
+  rc = forward_impl(idx0, idx1, 2, batch, max_active, nullptr, T, output_size, bias, out0, out1, s, &t);
+  if (rc != NNUE_OK) return rc;
+  if (cudaStreamWaitEvent(s, aux->join, 0) != cudaSuccess) return check_launch("forward_pair_tables_prepare: join");
+  return NNUE_OK;
+}
+
+int nnue_ft_backward_apply_tables(const float* grad0, const float* grad1, int64_t batch, int32_t max_active,
+                                  float* const* weight_grads, const int64_t* table_rows, int32_t n_tables,
+                                  int32_t output_size, float* bias_grad, int32_t accumulate, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  TableSet t;
+  int64_t T = 0;
+  int rc = make_tables("backward_apply_tables", weight_grads, table_rows, n_tables, t, T);
+  if (rc != NNUE_OK) return rc;
+  BwdPlan pl;
+  rc = make_plan(batch, max_active, T, output_size, 2, pl);
+  if (rc != NNUE_OK) return rc;
+  if (!bias_grad || (batch > 0 && (!grad0 || !grad1)))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "backward_apply_tables: null pointer");
+  if (!workspace || workspace_bytes < pl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(NNUE_ERR_WORKSPACE, "backward_apply_tables: workspace missing, misaligned or smaller than %zu bytes",
+                pl.total);
+  return apply_impl(grad0, grad1, pl, carve(pl, workspace), t.base[0], bias_grad, accumulate, 0, pl.T, true,
+                    static_cast<cudaStream_t>(stream), &t);
+}
+
+int nnue_ft_merge_virtual(const float* weight, int64_t rows, const float* virtual_weight, int64_t period,
+                          int32_t cols, float* out, void* stream) {
+  if (rows < 0 || cols < 0 || period <= 0 || rows % period != 0)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "merge_virtual: need rows a multiple of period > 0");
+  if (rows == 0 || cols == 0) return NNUE_OK;
+  if (!weight || !virtual_weight || !out) return fail(NNUE_ERR_INVALID_ARGUMENT, "merge_virtual: null pointer");
+  const bool v4 = cols % 4 == 0 && aligned16(weight) && aligned16(virtual_weight) && aligned16(out);
+  const int64_t row_vec = v4 ? cols / 4 : cols;
+  const int64_t n = rows * row_vec;
+  const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  count_launch();
+  if (v4)
+    merge_virtual_kernel<float4><<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(weight),
+                                                      reinterpret_cast<const float4*>(virtual_weight), n, row_vec,
+                                                      period, reinterpret_cast<float4*>(out));
+  else
+    merge_virtual_kernel<float><<<grid, 256, 0, s>>>(weight, virtual_weight, n, row_vec, period, out);
+  return check_launch("merge_virtual");
 }
 
 size_t nnue_ft_backward_workspace_size(int64_t batch, int32_t max_active, int64_t num_inputs, int32_t output_size,

@@ -224,3 +224,80 @@ def quantize_i16(x: torch.Tensor, scale: float) -> torch.Tensor:
     with torch.cuda.device(x.device):
         _native.call("nnue_ft_quantize_i16", x.data_ptr(), x.numel(), scale, q.data_ptr(), _stream_ptr(x.device))
     return q
+
+
+def _ptr_array(tensors):
+    import ctypes
+
+    return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() for t in tensors])
+
+
+def _rows_array(tensors):
+    import ctypes
+
+    return (ctypes.c_int64 * len(tensors))(*[t.shape[0] for t in tensors])
+
+
+def _check_tables(tables, dev, C, what):
+    if not 1 <= len(tables) <= 4:
+        raise ValueError(f"{what}: 1 to 4 tables supported, got {len(tables)}")
+    for i, t in enumerate(tables):
+        _check(t, f"{what}[{i}]", torch.float32, 2, dev)
+        if t.shape[1] != C:
+            raise ValueError(f"{what}[{i}] has {t.shape[1]} columns, expected {C}")
+
+
+def forward_pair_tables_prepare(idx0, idx1, tables, bias, out0, out1, workspace: torch.Tensor) -> None:
+    """forward_pair_prepare over a feature set whose rows are split over
+    separate tables (composed.py:49-54 without the torch.cat copy)."""
+    _check(idx0, "feature_indices_0", torch.int32, 2)
+    dev = idx0.device
+    _check(idx1, "feature_indices_1", torch.int32, 2, dev)
+    _check(bias, "bias", torch.float32, 1, dev)
+    C = bias.shape[0]
+    _check_tables(tables, dev, C, "tables")
+    _check(out0, "output_0", torch.float32, 2, dev)
+    _check(out1, "output_1", torch.float32, 2, dev)
+    if idx0.shape != idx1.shape:
+        raise ValueError("both perspectives need the same [batch, max_active] shape")
+    B, K = idx0.shape
+    if tuple(out0.shape) != (B, C) or tuple(out1.shape) != (B, C):
+        raise ValueError("output shapes do not match")
+    with torch.cuda.device(dev):
+        _native.call("nnue_ft_forward_pair_tables_prepare", idx0.data_ptr(), idx1.data_ptr(), B, K,
+                     _ptr_array(tables), _rows_array(tables), len(tables), C, bias.data_ptr(), out0.data_ptr(),
+                     out1.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream_ptr(dev))
+
+
+def backward_apply_tables(grad0, grad1, batch: int, max_active: int, weight_grads, bias_grad,
+                          workspace: torch.Tensor) -> None:
+    """Segment sums written straight into per-table gradients (every row)."""
+    dev = bias_grad.device
+    _check(bias_grad, "bias_grad", torch.float32, 1, dev)
+    C = bias_grad.shape[0]
+    _check_tables(weight_grads, dev, C, "weight_grads")
+    _check(grad0, "grad_output_0", torch.float32, 2, dev)
+    _check(grad1, "grad_output_1", torch.float32, 2, dev)
+    if tuple(grad0.shape) != (batch, C) or tuple(grad1.shape) != (batch, C):
+        raise ValueError("gradient shapes do not match")
+    with torch.cuda.device(dev):
+        _native.call("nnue_ft_backward_apply_tables", grad0.data_ptr(), grad1.data_ptr(), batch, max_active,
+                     _ptr_array(weight_grads), _rows_array(weight_grads), len(weight_grads), C, bias_grad.data_ptr(),
+                     0, workspace.data_ptr(), workspace.numel(), _stream_ptr(dev))
+
+
+def merge_virtual(weight: torch.Tensor, virtual_weight: torch.Tensor) -> torch.Tensor:
+    """weight + virtual_weight.repeat(weight.shape[0] // virtual rows, 1)
+    (halfka_v2_hm.py:69-70) in one pass, without the repeated copy."""
+    _check(weight, "weight", torch.float32, 2)
+    dev = weight.device
+    _check(virtual_weight, "virtual_weight", torch.float32, 2, dev)
+    R, C = weight.shape
+    Vr = virtual_weight.shape[0]
+    if virtual_weight.shape[1] != C or Vr == 0 or R % Vr:
+        raise ValueError("virtual_weight must have the weight's columns and a row count dividing its rows")
+    out = torch.empty_like(weight)
+    with torch.cuda.device(dev):
+        _native.call("nnue_ft_merge_virtual", weight.data_ptr(), R, virtual_weight.data_ptr(), Vr, C, out.data_ptr(),
+                     _stream_ptr(dev))
+    return out

@@ -409,10 +409,39 @@ def run_ours(args):
     # taken on smaller batches (profiles/); it does not scale with B (the
     # table re-reads stay near 1.3-1.4 GB), so no full-size figure is claimed.
     traffic = None
+    # Most row gathers hit L2, so the ceiling that bounds this kernel is the
+    # random 512-byte-row gather bandwidth from a table the size of one column
+    # slice of W (T rows x 512 B), measured here on this GPU
+    # (nnue_ft_gather_probe, 32 warps per SM, 8 rows in flight per warp).
+    n_warps, per_warp = 148 * 32, 2048
+    probe_rows = T
+    probe_table = torch.zeros(probe_rows * 128, device=dev)
+    probe_idx = torch.randint(0, probe_rows, (n_warps * per_warp,), dtype=torch.int32, device=dev,
+                              generator=torch.Generator(device=dev).manual_seed(args.seed + 7))
+    probe_out = torch.empty(n_warps * 128, device=dev)
+    stream_ptr = torch.cuda.current_stream(dev).cuda_stream
+
+    def probe():
+        _native.call("nnue_ft_gather_probe", probe_table.data_ptr(), probe_rows, probe_idx.data_ptr(), per_warp,
+                     n_warps, probe_out.data_ptr(), stream_ptr)
+
+    for _ in range(3):
+        probe()
+    pa, pb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pa.record()
+    for _ in range(5):
+        probe()
+    pb.record()
+    torch.cuda.synchronize()
+    gather_ceiling = n_warps * per_warp * 512 / (pa.elapsed_time(pb) / 5 / 1e3) / 1e9
+    del probe_table, probe_idx, probe_out
     roofline = {
         "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
         "traffic": traffic, "kernel": "ft_forward_kernel (forward pair, 1 launch per step)",
         "kernel_ms": kernel_ms, "algorithmic_bytes": a_fwd, "peak_source": f"{peak_src} hbm_gbs",
+        "l2_gather_ceiling": gather_ceiling, "frac_of_l2_gather_ceiling": achieved / gather_ceiling,
+        "l2_gather_ceiling_source": f"random 512-byte-row gathers from a {probe_rows * 512 / 1e6:.0f} MB table "
+                                    "(one column slice of W), measured in this run",
         "step_frac": a_step_survey / (ms_per_step / 1e3) / 1e9 / peak,
     }
 

@@ -153,8 +153,8 @@ int nnue_ft_forward_pair_prepare(const int32_t *idx0, const int32_t *idx1, int64
  *     someone else and no way to provide a workspace.
  *   - Limit: sizes whose nnue_ft_backward_workspace_size() exceeds
  *     nnue_ft_noalloc_scratch_bytes() are rejected with NNUE_ERR_UNSUPPORTED
- *     (HalfKAv2_hm, C = 1048: about 8K positions; Full_Threats+HalfKAv2_hm:
- *     a few thousand).
+ *     (C = 1048: about 9K HalfKAv2_hm positions, about 1.2K
+ *     Full_Threats+HalfKAv2_hm positions).
  *   - The array exists on every GPU that loads the library until the process
  *     exits.  The first call on each device looks up its device address
  *     (and, like nnue_ft_backward, creates the library's side stream); make

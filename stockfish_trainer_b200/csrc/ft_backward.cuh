@@ -630,6 +630,9 @@ struct SegParams {
   int32_t row_end;
   Geom g;
   TableSet dws;               // n > 1: dW split over separately allocated row blocks (dW unused)
+  float* heavy_part;          // [heavy_cap, 2, n_vec] vectors: per-perspective sums of heavy rows
+  unsigned* heavy_ticket;     // [heavy_cap, heavy_ticket_stride]: pair tickets (one per piece), zeroed per call
+  int32_t heavy_ticket_stride;
 };
 
 // Decodes a sorted value of perspective q; out-of-range values (a corrupt
@@ -779,8 +782,14 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_segsum_light_kernel(const Seg
   seg_write<VT, V>(p, f, c0 + lane, tot, ok, e1 > s0);
 }
 
-// Heavy rows of the fallback path: one warp per 32-vector piece of a column
-// chunk streams the row's dOut slices through a kHeavyStages-deep ring.
+// Heavy rows: a long sum per column whose only order-preserving parallelism
+// is across columns and across the two perspectives.  One warp per (row,
+// 32-vector piece of a column chunk, perspective) streams the segment's dOut
+// slices through a lane-private kHeavyStages-deep cp.async ring; the row's
+// positions are read 32 at a time, one group ahead of the ring, so the issue
+// side never waits for them.  With two perspectives each warp stores its sum
+// in `heavy_part` and the second of the pair to finish (a per-piece ticket,
+// zeroed before the launch; nobody waits) writes dW = acc_white + acc_black.
 constexpr int kHeavyWarps = 2;
 constexpr int kHeavyStages = 48;
 
@@ -794,8 +803,10 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
   const int c0 = p.g.begin(chunk);
   const int width = p.g.width(chunk);
   const int pieces = (width + 31) / 32;
+  const int P = p.P;
   const int wi = blockIdx.x * kHeavyWarps + warp;
-  const int slot = wi / pieces, piece = wi - slot * pieces;
+  const int q = wi % P;
+  const int slot = wi / P / pieces, piece = wi / P - slot * pieces;
   const int nh = *p.n_heavy < p.heavy_cap ? *p.n_heavy : p.heavy_cap;
   if (slot >= nh) return;
   const int64_t f = p.heavy_list[slot];
@@ -803,40 +814,59 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
   const int col = c0 + piece * 32 + lane;
   const bool ok1 = piece * 32 + lane < width;
   const int64_t row_vec = p.g.n_vec;
-
-  VT tot = Ops::zero();
-  for (int q = 0; q < p.P; ++q) {
-    const int s = p.seg_start[f * p.P + q], e = p.seg_start[f * p.P + q + 1];
-    const VT* src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]) + (ok1 ? col : 0);
-    VT acc = Ops::zero();
-    int t = s;  // issue pointer, kHeavyStages entries ahead of the consume pointer
-    int idx_base = -1, my_b = -1;
-    auto issue = [&](int slot_i) {
-      if (t < e) {
-        const int base = t & ~31;
-        if (base != idx_base) {
-          idx_base = base;
-          my_b = base + lane < e && base + lane >= s ? decode_position(__ldg(p.sorted_b + base + lane), q, p.B) : -1;
-        }
-        const int b = __shfl_sync(kFull, my_b, t & 31);
-        cp_async_vec<VT>(ring + slot_i * 32, src + (b >= 0 ? (int64_t)b * row_vec : 0), ok1 && b >= 0);
+  const int s = p.seg_start[f * P + q], e = p.seg_start[f * P + q + 1];
+  const VT* src = reinterpret_cast<const VT*>(q ? p.dout[1] : p.dout[0]) + (ok1 ? col : 0);
+  auto group = [&](int base) {  // decoded positions of entries [base, base + 32)
+    return base + lane < e ? decode_position(__ldg(p.sorted_b + base + lane), q, p.B) : -1;
+  };
+  VT acc = Ops::zero();
+  int t = s;  // issue pointer, kHeavyStages entries ahead of the consume pointer
+  int g_base = s, g_cur = group(s), g_next = group(s + 32);
+  auto issue = [&](int slot_i) {
+    if (t < e) {
+      if (t - g_base == 32) {  // next group of positions: already loaded; load the one after
+        g_base += 32;
+        g_cur = g_next;
+        g_next = group(g_base + 32);
       }
-      cp_async_commit();  // empty groups keep the pending count constant
-      ++t;
-    };
-    for (int i = 0; i < kHeavyStages; ++i) issue(i);
-    for (int j = s, stage = 0; j < e; ++j) {
-      cp_async_wait<kHeavyStages - 1>();
-      Ops::add(acc, ring[stage * 32]);
-      __syncwarp();
-      issue(stage);
-      stage = stage + 1 == kHeavyStages ? 0 : stage + 1;
+      const int b = __shfl_sync(kFull, g_cur, t - g_base);
+      cp_async_vec<VT>(ring + slot_i * 32, src + (b >= 0 ? (int64_t)b * row_vec : 0), ok1 && b >= 0);
     }
-    cp_async_wait<0>();
-    if (q == 0) tot = acc;
-    else Ops::add(tot, acc);
+    cp_async_commit();  // empty groups keep the pending count constant
+    ++t;
+  };
+  for (int i = 0; i < kHeavyStages; ++i) issue(i);
+  for (int j = s, stage = 0; j < e; ++j) {
+    cp_async_wait<kHeavyStages - 1>();
+    Ops::add(acc, ring[stage * 32]);
+    __syncwarp();
+    issue(stage);
+    stage = stage + 1 == kHeavyStages ? 0 : stage + 1;
   }
+  cp_async_wait<0>();
   const bool ok[1] = {ok1};
+  if (P == 1) {
+    const VT t1[1] = {acc};
+    seg_write<VT, 1>(p, f, col, t1, ok, true);
+    return;
+  }
+  // two perspectives: publish this half, the second finisher combines
+  VT* part = reinterpret_cast<VT*>(p.heavy_part) + ((int64_t)slot * 2 + q) * row_vec;
+  if (ok1) part[col] = acc;
+  __threadfence();
+  __syncwarp();
+  int ticket = 0;
+  unsigned* cnt = p.heavy_ticket + (int64_t)slot * p.heavy_ticket_stride + c0 + piece * 32;
+  if (lane == 0) ticket = (int)atomicAdd(cnt, 1u);
+  ticket = __shfl_sync(kFull, ticket, 0);
+  if (ticket != 1) return;
+  __threadfence();
+  const VT* other = reinterpret_cast<const VT*>(p.heavy_part) + ((int64_t)slot * 2 + (1 - q)) * row_vec;
+  VT tot = Ops::zero();
+  if (ok1) {
+    tot = __ldcg(other + col);  // the other warp's half, from L2
+    Ops::add(tot, acc);         // acc_white + acc_black (one fp32 add, order-free)
+  }
   const VT t1[1] = {tot};
   seg_write<VT, 1>(p, f, col, t1, ok, true);
 }

@@ -252,6 +252,7 @@ struct BwdPlan {
   int sort_variant = 0;
   size_t off_seg = 0, off_hist = 0, off_bsum = 0, off_ka = 0, off_va = 0, off_kb = 0, off_vb = 0;
   size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, off_first = 0, off_cursor = 0, off_big = 0;
+  size_t off_hpart = 0, off_hticket = 0;
   size_t total = 0;
 };
 
@@ -313,6 +314,8 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
   pl.off_first = take(sizeof(int32_t) * (pl.n_stream_warps + 1));
   pl.off_cursor = take(pl.sort_variant == 1 ? sizeof(int32_t) * pl.NK : 0);
   pl.off_big = take(pl.sort_variant == 1 ? sizeof(int32_t) * (pl.NK + 1) : 0);
+  pl.off_hpart = take(P == 2 ? sizeof(float) * pl.heavy_cap * 2 * C : 0);
+  pl.off_hticket = take(P == 2 ? sizeof(uint32_t) * pl.heavy_cap * C : 0);
   pl.total = o;
   return NNUE_OK;
 }
@@ -323,6 +326,8 @@ struct Ws {
   double* partial;
   int32_t* first_row;
   int32_t *cursor, *big;
+  float* hpart;
+  uint32_t* hticket;
 };
 
 Ws carve(const BwdPlan& pl, void* base) {
@@ -342,6 +347,8 @@ Ws carve(const BwdPlan& pl, void* base) {
   w.first_row = reinterpret_cast<int32_t*>(b + pl.off_first);
   w.cursor = reinterpret_cast<int32_t*>(b + pl.off_cursor);
   w.big = reinterpret_cast<int32_t*>(b + pl.off_big);
+  w.hpart = reinterpret_cast<float*>(b + pl.off_hpart);
+  w.hticket = reinterpret_cast<uint32_t*>(b + pl.off_hticket);
   return w;
 }
 
@@ -505,7 +512,7 @@ int launch_segsum_heavy(SegParams p, cudaStream_t s) {
     return check_launch("backward_apply: heavy kernel shared memory");
   const int pieces_max = lanes_per_row(p.g);
   p.chunk0 = 0;
-  dim3 grid((unsigned)ceil_div((int64_t)p.heavy_cap * pieces_max, kHeavyWarps), (unsigned)p.g.n_chunks);
+  dim3 grid((unsigned)ceil_div((int64_t)p.heavy_cap * pieces_max * p.P, kHeavyWarps), (unsigned)p.g.n_chunks);
   count_launch();
   ft_segsum_heavy_kernel<VT><<<grid, 32 * kHeavyWarps, smem, s>>>(p);
   return NNUE_OK;
@@ -618,10 +625,13 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   p.row_end = (int32_t)row_end;
   if (dws && dws->n > 1) p.dws = *dws;
   else p.dws.n = 1;
+  p.heavy_part = w.hpart;
+  p.heavy_ticket = w.hticket;
   if (dws && dws->n == 1) p.dW = dws->base[0];
   p.g = v4 ? make_geom(pl.C / 4, g_tune.bwd_chunk_vec, g_tune.bwd_exact_chunks)
              : make_geom(pl.C, g_tune.bwd_chunk_vec * 4, g_tune.bwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "backward: column chunk too wide");
+  p.heavy_ticket_stride = p.g.n_vec;
   if (pl.B * (int64_t)p.g.n_vec > INT32_MAX)
     return fail(NNUE_ERR_UNSUPPORTED, "backward: grad_output exceeds 2^31 %s per perspective",
                 v4 ? "16-byte vectors" : "floats");
@@ -638,6 +648,9 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
       return check_launch("backward_apply: fork");
     if (!stream && rows) {
+      if (pl.P == 2 && pl.heavy_cap > 0 &&
+          cudaMemsetAsync(w.hticket, 0, sizeof(uint32_t) * pl.heavy_cap * p.g.n_vec, aux->side) != cudaSuccess)
+        return check_launch("backward_apply: heavy tickets");
       rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
       if (rc != NNUE_OK) return rc;
     }

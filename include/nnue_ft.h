@@ -151,8 +151,7 @@ int nnue_ft_forward_pair_prepare(const int32_t *idx0, const int32_t *idx1, int64
  *     call, e.g. a search / inference loop on a fixed memory budget, or a
  *     host that reaches the GPU only through this C ABI with tensors owned by
  *     someone else and no way to provide a workspace.
- *   - Limit: sizes whose backward scratch (nnue_ft_backward_workspace_size()
- *     less the region only nnue_ft_forward_pair_prepare uses) exceeds
+ *   - Limit: sizes whose nnue_ft_backward_workspace_size() exceeds
  *     nnue_ft_noalloc_scratch_bytes() are rejected with NNUE_ERR_UNSUPPORTED
  *     (C = 1048: about 9K HalfKAv2_hm positions, about 1.2K
  *     Full_Threats+HalfKAv2_hm positions).

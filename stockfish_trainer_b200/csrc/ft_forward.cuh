@@ -33,8 +33,6 @@ struct FwdParams {
   int32_t chunk0;          // first column chunk of this launch (blockIdx.y offset)
   Geom g;
   TableSet tabs;           // MULTI kernels: W split over separately allocated row blocks
-  int32_t* cidx;           // [P * B, K] compacted row offsets, -1 terminated (cmode 1 writes, 2 reads)
-  int32_t cmode;           // 0: compact the raw indices; 1: and write them to cidx; 2: read cidx instead
 };
 
 constexpr int kIdxGroups = 8;  // index slots read per item in one go: 8 x 32 = 256
@@ -42,35 +40,12 @@ constexpr int kIdxGroups = 8;  // index slots read per item in one go: 8 x 32 = 
 // Loads slots [32 * g0, 32 * (g0 + kIdxGroups)) of one index row, one group of
 // 32 per register, all loads in flight together.
 __device__ __forceinline__ void load_index_groups(const int32_t* __restrict__ irow, int K, int g0, int lane,
-                                                  int (&f)[kIdxGroups], int gmax = kIdxGroups) {
+                                                  int (&f)[kIdxGroups]) {
 #pragma unroll
   for (int g = 0; g < kIdxGroups; ++g) {
     const int k = (g0 + g) * 32 + lane;
-    f[g] = k < K && g < gmax ? __ldcs(irow + k) : -1;
+    f[g] = k < K ? __ldcs(irow + k) : -1;
   }
-}
-
-// Compacted list of one item (cmode 2): the first n entries before the -1
-// terminator (or all K) are row offsets; groups past those loaded in f[] are
-// fetched on demand.  Copies them to `list`; returns n.
-__device__ __forceinline__ int read_compacted(const int32_t* __restrict__ crow, int K, int (&f)[kIdxGroups],
-                                              int gloaded, int* list, int lane) {
-  const int ng = (K + 31) / 32;
-  int n = K;
-#pragma unroll
-  for (int g = 0; g < kIdxGroups; ++g) {
-    if (g >= ng) break;
-    if (g >= gloaded) f[g] = g * 32 + lane < K ? __ldcs(crow + g * 32 + lane) : -1;
-    const unsigned m = __ballot_sync(kFull, f[g] == -1 || g * 32 + lane >= K);
-    const int end = m ? g * 32 + __ffs(m) - 1 : g * 32 + 32;
-    if (g * 32 + lane < end) list[g * 32 + lane] = f[g];
-    if (m) {
-      n = end;
-      break;
-    }
-  }
-  __syncwarp();
-  return n < K ? n : K;
 }
 
 // Writes the valid indices of f[] (ascending slot order), times `scale`, to
@@ -147,13 +122,8 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
     return (q ? p.idx[1] : p.idx[0]) + (it - (int64_t)q * p.B) * p.K;
   };
   const int n_super = (p.K + 32 * kIdxGroups - 1) / (32 * kIdxGroups);
-  // cmode 2 reads the compacted lists of an earlier launch (K <= 256): only
-  // the first two groups are prefetched, the rest (long items) on demand
-  const bool read_c = !MULTI && p.cmode == 2;
-  const int gpre = read_c ? 2 : kIdxGroups;
-  auto src_row = [&](int64_t it) -> const int32_t* { return read_c ? p.cidx + it * p.K : index_row(it); };
   int f[kIdxGroups];
-  load_index_groups(src_row(item), p.K, 0, lane, f, gpre);
+  load_index_groups(index_row(item), p.K, 0, lane, f);
 
   for (; item < item_end; ++item) {
     const int persp = item >= p.B ? 1 : 0;
@@ -165,20 +135,10 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
     for (int sg = 0; sg < n_super; ++sg) {
       if (sg > 0) load_index_groups(irow, p.K, sg * kIdxGroups, lane, f);
       int n;
-      if constexpr (MULTI) {
-        n = compact_rows<VT>(f, p.T, p.tabs, row_vec, c0, list, lane);
-      } else if (read_c) {
-        n = read_compacted(p.cidx + item * p.K, p.K, f, gpre, list, lane);
-      } else {
-        n = compact_valid(f, p.T, list, lane, row_vec);
-        if (p.cmode == 1) {  // publish the compacted offsets for the later column chunks
-          int32_t* crow = p.cidx + item * p.K;
-          for (int k = lane; k < n; k += 32) crow[k] = list[k];
-          if (lane == 0 && n < p.K) crow[n] = -1;
-        }
-      }
+      if constexpr (MULTI) n = compact_rows<VT>(f, p.T, p.tabs, row_vec, c0, list, lane);
+      else n = compact_valid(f, p.T, list, lane, row_vec);
       // the next item's indices load while this item's rows are in flight
-      if (sg == n_super - 1 && item + 1 < item_end) load_index_groups(src_row(item + 1), p.K, 0, lane, f, gpre);
+      if (sg == n_super - 1 && item + 1 < item_end) load_index_groups(index_row(item + 1), p.K, 0, lane, f);
       VT w[D][V];
       auto row_ptr = [&](const Entry e) -> const VT* {
         if constexpr (MULTI) return e + lane;

@@ -51,7 +51,6 @@ struct Tuning {
   int64_t fwd_chunk_vec = 32;       // forward column chunk, in 16-byte vectors
   int64_t fwd_items_per_warp = 16;  // (perspective, position) items per warp
   int64_t fwd_unroll = 6;          // table rows in flight per warp (4, 6 or 8)
-  int64_t fwd_compact_idx = 1;     // with a workspace and K > 64: chunk 0 publishes compacted indices
   int64_t bwd_unroll = 2;          // dOut rows per batch, light rows (2, 4 or 8)
   int64_t bwd_entries_per_warp = 2048;  // streaming backward: sorted entries per warp
   int64_t fwd_min_blocks = 4;      // forward: registers sized for 2..6 resident blocks (chunks <= 64 vectors)
@@ -95,7 +94,6 @@ ParamRef* params() {
       {"heavy_cap", &g_tune.heavy_cap, 0, 1 << 24},
       {"sort_tile_rows", &g_tune.sort_tile_rows, 1, 1 << 16},
       {"sort_variant", &g_tune.sort_variant, 0, 1},
-      {"fwd_compact_idx", &g_tune.fwd_compact_idx, 0, 1},
       {"sort_blocks_per_sm", &g_tune.sort_blocks_per_sm, 1, 1 << 16},
       {"sort_tile", &g_tune.sort_tile, 32 * kSortBatch, 1 << 20},
       {"colsum_parts", &g_tune.colsum_parts, 1, 1 << 16},
@@ -177,16 +175,6 @@ void launch_forward_range(const FwdParams& p, int chunk0, int n_chunks, int widt
 
 template <typename VT>
 void launch_forward(const FwdParams& p, cudaStream_t s) {
-  if (p.cidx && p.g.n_chunks > 1) {
-    // chunk 0 compacts the indices and publishes them; the other chunks read
-    // the compacted lists (stream order makes them complete)
-    FwdParams a = p, b = p;
-    a.cmode = 1;
-    b.cmode = 2;
-    launch_forward_range<VT>(a, 0, 1, p.g.width(0), s);
-    launch_forward_range<VT>(b, 1, p.g.n_chunks - 1, p.g.max_width, s);
-    return;
-  }
   launch_forward_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
 }
 
@@ -218,7 +206,7 @@ bool tables_aligned16(const TableSet& t) {
 
 int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int32_t K, const float* W,
                  int64_t T, int32_t C, const float* bias, float* out0, float* out1, cudaStream_t s,
-                 const TableSet* tabs = nullptr, int32_t* cidx = nullptr) {
+                 const TableSet* tabs = nullptr) {
   if (B < 0 || K < 0 || T < 0 || C <= 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "forward: bad sizes");
   if (T > INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "forward: num_inputs exceeds int32 index range");
   if (B == 0) return NNUE_OK;
@@ -241,8 +229,6 @@ int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int
   if (tabs && tabs->n > 1) p.tabs = *tabs;
   else p.tabs.n = 1;
   if (tabs && tabs->n == 1) p.W = tabs->base[0];
-  // compacted-index reuse: single table, one index super-group (K <= 256)
-  p.cidx = (cidx && p.tabs.n == 1 && K <= 32 * kIdxGroups) ? cidx : nullptr;
   p.g = v4 ? make_geom(C / 4, g_tune.fwd_chunk_vec, g_tune.fwd_exact_chunks)
              : make_geom(C, g_tune.fwd_chunk_vec * 4, g_tune.fwd_exact_chunks);
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "forward: column chunk too wide");
@@ -266,16 +252,11 @@ struct BwdPlan {
   int sort_variant = 0;
   size_t off_seg = 0, off_hist = 0, off_bsum = 0, off_ka = 0, off_va = 0, off_kb = 0, off_vb = 0;
   size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, off_first = 0, off_cursor = 0, off_big = 0;
-  size_t off_hpart = 0, off_hticket = 0, off_cidx = 0;
+  size_t off_hpart = 0, off_hticket = 0;
   size_t total = 0;
 };
 
-// The compacted-index region (for nnue_ft_forward_pair_prepare) is the last
-// region of the layout, so plans with and without it agree on every other
-// offset.  Only nnue_ft_forward_pair_prepare uses it, and the workspace-size
-// query reports the size with it; every other entry point accepts the
-// smaller total.
-int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl, bool with_fwd_indices = false) {
+int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl) {
   if (P != 1 && P != 2) return fail(NNUE_ERR_INVALID_ARGUMENT, "backward: n_persp must be 1 or 2");
   if (B < 0 || K < 0 || T <= 0 || C <= 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "backward: bad sizes");
   pl.B = B;
@@ -335,10 +316,6 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
   pl.off_big = take(pl.sort_variant == 1 ? sizeof(int32_t) * (pl.NK + 1) : 0);
   pl.off_hpart = take(P == 2 ? sizeof(float) * pl.heavy_cap * 2 * C : 0);
   pl.off_hticket = take(P == 2 ? sizeof(uint32_t) * pl.heavy_cap * C : 0);
-  // the forward's later column chunks read chunk 0's compacted indices (a
-  // -1 padded 160-slot row holds ~41 valid entries: 2.5x less index traffic)
-  if (with_fwd_indices && g_tune.fwd_compact_idx && K > 64 && K <= 256)
-    pl.off_cidx = take(sizeof(int32_t) * pl.nnz_max);
   pl.total = o;
   return NNUE_OK;
 }
@@ -351,7 +328,6 @@ struct Ws {
   int32_t *cursor, *big;
   float* hpart;
   uint32_t* hticket;
-  int32_t* cidx;
 };
 
 Ws carve(const BwdPlan& pl, void* base) {
@@ -373,7 +349,6 @@ Ws carve(const BwdPlan& pl, void* base) {
   w.big = reinterpret_cast<int32_t*>(b + pl.off_big);
   w.hpart = reinterpret_cast<float*>(b + pl.off_hpart);
   w.hticket = reinterpret_cast<uint32_t*>(b + pl.off_hticket);
-  w.cidx = pl.off_cidx ? reinterpret_cast<int32_t*>(b + pl.off_cidx) : nullptr;
   return w;
 }
 
@@ -843,7 +818,7 @@ int nnue_ft_forward_pair_prepare(const int32_t* idx0, const int32_t* idx1, int64
                                  const float* weight, int64_t num_inputs, int32_t output_size, const float* bias,
                                  float* out0, float* out1, void* workspace, size_t workspace_bytes, void* stream) {
   BwdPlan pl;
-  int rc = make_plan(batch, max_active, num_inputs, output_size, 2, pl, true);
+  int rc = make_plan(batch, max_active, num_inputs, output_size, 2, pl);
   if (rc != NNUE_OK) return rc;
   rc = check_bwd_args(idx0, idx1, 2, workspace, workspace_bytes, pl);
   if (rc != NNUE_OK) return rc;
@@ -861,8 +836,7 @@ int nnue_ft_forward_pair_prepare(const int32_t* idx0, const int32_t* idx1, int64
     if (rc != NNUE_OK) return rc;
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("forward_pair_prepare: join record");
   }
-  rc = forward_impl(idx0, idx1, 2, batch, max_active, weight, num_inputs, output_size, bias, out0, out1, s, nullptr,
-                    pl.off_cidx ? carve(pl, workspace).cidx : nullptr);
+  rc = forward_impl(idx0, idx1, 2, batch, max_active, weight, num_inputs, output_size, bias, out0, out1, s);
   if (rc != NNUE_OK) return rc;
   if (cudaStreamWaitEvent(s, aux->join, 0) != cudaSuccess) return check_launch("forward_pair_prepare: join");
   return NNUE_OK;
@@ -955,7 +929,7 @@ int nnue_ft_merge_virtual(const float* weight, int64_t rows, const float* virtua
 size_t nnue_ft_backward_workspace_size(int64_t batch, int32_t max_active, int64_t num_inputs, int32_t output_size,
                                        int32_t n_persp) {
   BwdPlan pl;
-  if (make_plan(batch, max_active, num_inputs, output_size, n_persp, pl, true) != NNUE_OK) return 0;
+  if (make_plan(batch, max_active, num_inputs, output_size, n_persp, pl) != NNUE_OK) return 0;
   return pl.total;
 }
 

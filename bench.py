@@ -44,6 +44,13 @@ METRIC = "positions/s FT fwd+bwd @B=65536 L1=1040, 1/2/4/8 B200; % HBM roofline"
 FEATURE_SET = "Full_Threats+HalfKAv2_hm^"
 L1, NPSQT = 1040, 8
 C = L1 + NPSQT
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# gather kernels in the default 1-GPU headline run, from a one-pass ncu
+# capture of that command (profiles/dram_traffic_headline_fullsize.md).
+TRAFFIC_HEADLINE: dict = {
+    "ft_forward_kernel": 1.7705e9 + 0.5321e9,
+    "ft_segsum_light_kernel": 1.7176e9 + 0.3473e9,
+}
 DATA = ("synthetic: seeded random positions (kings + U{0..30} pieces), indices from the native restatement "
         "of the reference feature functions; W~N(0,0.01), bias=0, dOut~N(0,1)")
 
@@ -355,6 +362,10 @@ def run_ours(args):
     clocks = ClockSampler(rt.local_rank) if rank == 0 else None
     time.sleep(0.3)  # let the sampler start
     barrier()
+    # every launch of the gather kernels inside the timed steps is bracketed by
+    # a CUDA event pair on its own stream (nnue_ft_kernel_timer_arm)
+    timed_kinds = (_native.TIMED_FORWARD, _native.TIMED_LIGHT_ROWS, _native.TIMED_HEAVY_ROWS)
+    _native.kernel_timer_arm(timed_kinds, (2 + 2 * max(args.ddp_blocks, 1)) * args.steps + 16)
     l0 = _native.launch_count()
     if clocks:
         clocks.mark()
@@ -367,6 +378,8 @@ def run_ours(args):
     if clocks:
         clocks.mark()
     launches = _native.launch_count() - l0
+    live = {k: _native.kernel_timer_read(k) for k in timed_kinds}
+    _native.kernel_timer_arm((), 0)
     ms_local = start.elapsed_time(end)
     ms = max_over_ranks(ms_local)
     # with --ddp-blocks the "backward_apply" phase includes the overlapped allreduce
@@ -385,16 +398,46 @@ def run_ours(args):
     ms_per_step = ms / args.steps
     value = args.batch / (ms_per_step / 1e3)
 
-    # ---- roofline: the forward pair launch (one kernel, both perspectives) ---
-    # Its duration is taken with CUDA events on the launching stream over
-    # K launches of the kernel alone, right after the timed steps (inside the
-    # step it shares the GPU with the concurrent index phase, so the phase
-    # time would overstate it).  Algorithmic bytes per launch: every active
-    # row gathered once + outputs written + indices read + bias.
+    # ---- roofline: the gather kernels, timed live inside the timed steps ----
+    # Durations come from the event pairs recorded around each launch on its
+    # own stream (so they include the concurrent side-stream work of the real
+    # step).  The roofline object describes the kernel with the largest time
+    # per step; "kernels" lists all three.  Algorithmic bytes per launch:
+    #   forward: every active row gathered once + outputs written + indices
+    #            read + bias;
+    #   light rows: the dOut rows of the light rows' entries gathered + their
+    #            positions + segment bounds and row kinds of all rows + every
+    #            light row of dW written once;
+    #   heavy rows: the same for the heavy rows.
     peak, peak_src = hbm_peak()
+    counts = np.bincount(white[white >= 0], minlength=T) + np.bincount(black[black >= 0], minlength=T)
+    heavy = np.sort(counts[counts > _native.get_param("heavy_threshold")])[::-1][:_native.get_param("heavy_cap")]
+    n_heavy, nnz_heavy = int(heavy.size), int(heavy.sum())
+    nnz_light = nnz_rank - nnz_heavy
     a_fwd = nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4 + C * 4
+    a_light = nnz_light * (C * 4 + 4) + (2 * T + 1) * 4 + T + (T - n_heavy) * C * 4
+    a_heavy = nnz_heavy * (C * 4 + 4) + n_heavy * C * 4
     a_step_survey = (nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4) + \
                     (nnz_rank * C * 4 + 2 * b_rank * K * 4 + T * C * 4)
+    # DRAM bytes per launch from a one-pass ncu capture of this exact command
+    # (profiles/dram_traffic_headline_fullsize.md); other shapes: not captured
+    traffic_ref = TRAFFIC_HEADLINE if (args.workload == "headline" and b_rank == 65536 and not args.param
+                                       and world == 1) else {}
+    kernels = {}
+    for kind, name, a_bytes in ((_native.TIMED_FORWARD, "ft_forward_kernel", a_fwd),
+                                (_native.TIMED_LIGHT_ROWS, "ft_segsum_light_kernel", a_light),
+                                (_native.TIMED_HEAVY_ROWS, "ft_segsum_heavy_kernel", a_heavy)):
+        durations = live[kind]
+        # every rank takes part in the max, launched or not
+        per_step_ms = max_over_ranks(float(np.sum(durations)) / args.steps if durations else 0.0)
+        if per_step_ms <= 0.0:
+            continue
+        launches_per_step = len(durations) / args.steps
+        achieved_k = a_bytes / (per_step_ms / 1e3) / 1e9
+        kernels[name] = {"ms_per_step": per_step_ms, "launches_per_step": launches_per_step,
+                         "algorithmic_bytes": a_bytes, "achieved": achieved_k, "frac": achieved_k / peak,
+                         "traffic": traffic_ref.get(name)}
+    # the forward alone, K launches with nothing beside it
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(max(args.steps, 1))]
     barrier()
@@ -403,13 +446,10 @@ def run_ours(args):
         ops.forward_pair_into(i0, i1, W, bias, out0, out1)
         b.record()
     barrier()
-    kernel_ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in kev])))
-    achieved = a_fwd / (kernel_ms / 1e3) / 1e9
-    # DRAM traffic per launch needs a multi-pass ncu capture, which is only
-    # taken on smaller batches (profiles/); it does not scale with B (the
-    # table re-reads stay near 1.3-1.4 GB), so no full-size figure is claimed.
-    traffic = None
-    # Most row gathers hit L2, so the ceiling that bounds this kernel is the
+    fwd_alone_ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in kev])))
+    if "ft_forward_kernel" in kernels:
+        kernels["ft_forward_kernel"]["ms_alone"] = fwd_alone_ms
+    # Most row gathers hit L2, so the ceiling that bounds these kernels is the
     # random 512-byte-row gather bandwidth from a table the size of one column
     # slice of W (T rows x 512 B), measured here on this GPU
     # (nnue_ft_gather_probe, 32 warps per SM, 8 rows in flight per warp).
@@ -435,15 +475,21 @@ def run_ours(args):
     torch.cuda.synchronize()
     gather_ceiling = n_warps * per_warp * 512 / (pa.elapsed_time(pb) / 5 / 1e3) / 1e9
     del probe_table, probe_idx, probe_out
-    roofline = {
-        "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-        "traffic": traffic, "kernel": "ft_forward_kernel (forward pair, 1 launch per step)",
-        "kernel_ms": kernel_ms, "algorithmic_bytes": a_fwd, "peak_source": f"{peak_src} hbm_gbs",
-        "l2_gather_ceiling": gather_ceiling, "frac_of_l2_gather_ceiling": achieved / gather_ceiling,
-        "l2_gather_ceiling_source": f"random 512-byte-row gathers from a {probe_rows * 512 / 1e6:.0f} MB table "
-                                    "(one column slice of W), measured in this run",
-        "step_frac": a_step_survey / (ms_per_step / 1e3) / 1e9 / peak,
-    }
+    for k in kernels.values():
+        k["frac_of_l2_gather_ceiling"] = k["achieved"] / gather_ceiling
+    top = max(kernels, key=lambda k: kernels[k]["ms_per_step"]) if kernels else None
+    roofline = {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_source": f"{peak_src} hbm_gbs",
+                "l2_gather_ceiling": gather_ceiling,
+                "l2_gather_ceiling_source": f"random 512-byte-row gathers from a {probe_rows * 512 / 1e6:.0f} MB "
+                                            "table (one column slice of W), measured in this run",
+                "step_frac": a_step_survey / (ms_per_step / 1e3) / 1e9 / peak}
+    if top:
+        k = kernels[top]
+        roofline.update({"achieved": k["achieved"], "frac": k["frac"], "traffic": k["traffic"],
+                         "kernel": f"{top} (largest device time per step, timed live in the step)",
+                         "kernel_ms": k["ms_per_step"], "algorithmic_bytes": k["algorithmic_bytes"],
+                         "frac_of_l2_gather_ceiling": k["frac_of_l2_gather_ceiling"]})
+    roofline["kernels"] = kernels
 
     # ---- e2e through the reference-facing autograd API, host buffers -------
     e2e = None

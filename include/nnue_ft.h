@@ -53,6 +53,21 @@ int nnue_ft_version(void);
  * devices, all threads); lets a caller count launches inside a region. */
 uint64_t nnue_ft_launch_count(void);
 
+/* Per-launch timing of the gather kernels (measurement support; no
+ * reference counterpart).  Arms the kernel classes in the bit mask `kernels`
+ * (1: forward gather kernel, 2: light-row segment-sum kernel, 4: heavy-row
+ * segment-sum kernel) for up to `capacity` timed launches in total on the
+ * current device: each launch of an armed class is bracketed by a CUDA event
+ * pair recorded on the stream it is launched on, so its duration includes
+ * whatever runs concurrently on other streams.  kernels == 0 disarms and
+ * frees the events.  Not for use under stream capture. */
+int nnue_ft_kernel_timer_arm(uint32_t kernels, int32_t capacity);
+
+/* Waits for the timed launches of class `kernel` (0 forward, 1 light rows,
+ * 2 heavy rows) and writes up to `max` durations in milliseconds, in launch
+ * order; *count receives the number of timed launches of that class. */
+int nnue_ft_kernel_timer_read(int32_t kernel, float *ms, int32_t max, int32_t *count);
+
 /* Message for the last failing call on this thread ("" if none). */
 const char *nnue_ft_last_error(void);
 

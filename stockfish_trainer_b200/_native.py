@@ -32,6 +32,8 @@ DEVERR_BAD_PSQT_INDEX = 8
 _SIGNATURES = {
     "nnue_ft_version": (_I32, []),
     "nnue_ft_launch_count": (_U64, []),
+    "nnue_ft_kernel_timer_arm": (_I32, [ctypes.c_uint32, _I32]),
+    "nnue_ft_kernel_timer_read": (_I32, [_I32, ctypes.POINTER(ctypes.c_float), _I32, ctypes.POINTER(_I32)]),
     "nnue_ft_last_error": (ctypes.c_char_p, []),
     "nnue_ft_device_errors": (_I32, [ctypes.POINTER(ctypes.c_uint32), _I32]),
     "nnue_ft_set_param": (_I32, [ctypes.c_char_p, _I64]),
@@ -130,6 +132,27 @@ def call(func: str, *args) -> int:
 def launch_count() -> int:
     """Kernels launched by the native library so far (process-wide)."""
     return int(load().nnue_ft_launch_count())
+
+
+TIMED_FORWARD, TIMED_LIGHT_ROWS, TIMED_HEAVY_ROWS = 0, 1, 2
+
+
+def kernel_timer_arm(kernels, capacity: int) -> None:
+    """Time every launch of the given kernel classes (TIMED_* values) with a
+    CUDA event pair on its own stream, up to `capacity` launches in total;
+    an empty `kernels` disarms."""
+    mask = 0
+    for k in kernels:
+        mask |= 1 << int(k)
+    call("nnue_ft_kernel_timer_arm", mask, int(capacity))
+
+
+def kernel_timer_read(kernel: int, max_launches: int = 4096) -> list:
+    """Durations (ms) of the timed launches of one kernel class, in order."""
+    buf = (ctypes.c_float * max(max_launches, 1))()
+    n = _I32(0)
+    call("nnue_ft_kernel_timer_read", int(kernel), buf, int(max_launches), ctypes.byref(n))
+    return [float(buf[i]) for i in range(min(n.value, max_launches))]
 
 
 def set_param(name: str, value: int) -> None:

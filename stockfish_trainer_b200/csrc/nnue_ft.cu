@@ -13,6 +13,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/nnue_ft.h"
 #include "common.cuh"
@@ -29,6 +30,45 @@ thread_local std::string g_last_error;
 std::atomic<unsigned long long> g_launches{0};  // kernel launches issued by this library
 
 inline void count_launch(unsigned n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// Optional per-launch timing of the gather kernels (measurement support, off
+// by default).  When a kernel class is armed, a CUDA event pair is recorded
+// on the launching stream around each launch of that class, so a caller can
+// read the kernel's own duration inside a real step, with whatever runs
+// concurrently on other streams.  Not for use under stream capture.
+enum TimedKernel : int { kTimeForward = 0, kTimeLight = 1, kTimeHeavy = 2, kTimedKinds = 3 };
+struct KernelTimer {
+  std::mutex mu;
+  std::atomic<unsigned> mask{0};
+  std::vector<cudaEvent_t> start, stop;  // capacity pairs, created when armed
+  std::vector<int> kind;                 // class of each recorded pair
+  void release() {
+    for (cudaEvent_t e : start) cudaEventDestroy(e);
+    for (cudaEvent_t e : stop) cudaEventDestroy(e);
+    start.clear();
+    stop.clear();
+    kind.clear();
+    mask = 0;
+  }
+};
+KernelTimer g_timer;
+
+// Records the start event of a timed launch; returns the pair's slot or -1.
+int timer_begin(int k, cudaStream_t s) {
+  if (!(g_timer.mask.load(std::memory_order_relaxed) & (1u << k))) return -1;  // unarmed: no lock
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  const size_t i = g_timer.kind.size();
+  if (!(g_timer.mask.load() & (1u << k)) || i >= g_timer.start.size()) return -1;
+  if (cudaEventRecord(g_timer.start[i], s) != cudaSuccess) return -1;
+  g_timer.kind.push_back(k);
+  return (int)i;
+}
+
+void timer_end(int slot, cudaStream_t s) {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  if ((size_t)slot < g_timer.stop.size()) cudaEventRecord(g_timer.stop[slot], s);
+}
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -175,7 +215,9 @@ void launch_forward_range(const FwdParams& p, int chunk0, int n_chunks, int widt
 
 template <typename VT>
 void launch_forward(const FwdParams& p, cudaStream_t s) {
+  const int slot = timer_begin(kTimeForward, s);
   launch_forward_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
+  timer_end(slot, s);
 }
 
 // Builds a table set from per-block pointers and row counts (n_tables >= 1).
@@ -494,7 +536,9 @@ void launch_segsum_range(const SegParams& p, int chunk0, int n_chunks, int width
 
 template <typename VT>
 void launch_segsum_light(const SegParams& p, cudaStream_t s) {
+  const int slot = timer_begin(kTimeLight, s);
   launch_segsum_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
+  timer_end(slot, s);
 }
 
 template <typename VT>
@@ -514,7 +558,9 @@ int launch_segsum_heavy(SegParams p, cudaStream_t s) {
   p.chunk0 = 0;
   dim3 grid((unsigned)ceil_div((int64_t)p.heavy_cap * pieces_max * p.P, kHeavyWarps), (unsigned)p.g.n_chunks);
   count_launch();
+  const int slot = timer_begin(kTimeHeavy, s);
   ft_segsum_heavy_kernel<VT><<<grid, 32 * kHeavyWarps, smem, s>>>(p);
+  timer_end(slot, s);
   return NNUE_OK;
 }
 
@@ -763,6 +809,46 @@ extern "C" {
 int nnue_ft_version(void) { return 100; }
 
 uint64_t nnue_ft_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int nnue_ft_kernel_timer_arm(uint32_t kernels, int32_t capacity) {
+  if (kernels >= (1u << kTimedKinds) || capacity < 0 || (kernels && capacity == 0))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "kernel_timer_arm: bad kernel mask %u or capacity %d", kernels,
+                (int)capacity);
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  g_timer.release();
+  if (!kernels) return NNUE_OK;
+  for (int32_t i = 0; i < capacity; ++i) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
+      if (a) cudaEventDestroy(a);
+      g_timer.release();
+      return check_launch("kernel_timer_arm: event create");
+    }
+    g_timer.start.push_back(a);
+    g_timer.stop.push_back(b);
+  }
+  g_timer.kind.reserve(capacity);
+  g_timer.mask.store(kernels);
+  return NNUE_OK;
+}
+
+int nnue_ft_kernel_timer_read(int32_t kernel, float* ms, int32_t max, int32_t* count) {
+  if (kernel < 0 || kernel >= kTimedKinds || !count || max < 0 || (max > 0 && !ms))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "kernel_timer_read: bad arguments");
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  int32_t n = 0;
+  for (size_t i = 0; i < g_timer.kind.size(); ++i) {
+    if (g_timer.kind[i] != kernel) continue;
+    if (n < max) {
+      if (cudaEventSynchronize(g_timer.stop[i]) != cudaSuccess ||
+          cudaEventElapsedTime(&ms[n], g_timer.start[i], g_timer.stop[i]) != cudaSuccess)
+        return check_launch("kernel_timer_read");
+    }
+    ++n;
+  }
+  *count = n;
+  return NNUE_OK;
+}
 
 const char* nnue_ft_last_error(void) { return g_last_error.c_str(); }
 

@@ -74,3 +74,16 @@ def test_workspace_size_grows_with_batch():
     a = lib.nnue_ft_backward_workspace_size(1024, 160, 85296, 1048, 2)
     b = lib.nnue_ft_backward_workspace_size(4096, 160, 85296, 1048, 2)
     assert 0 < a < b
+
+
+def test_kernel_timer_arguments():
+    lib = _native.load()
+    # bad mask / capacity are rejected before any CUDA call
+    assert lib.nnue_ft_kernel_timer_arm(8, 4) == _native.NNUE_ERR_INVALID_ARGUMENT
+    assert lib.nnue_ft_kernel_timer_arm(1, -1) == _native.NNUE_ERR_INVALID_ARGUMENT
+    assert lib.nnue_ft_kernel_timer_arm(1, 0) == _native.NNUE_ERR_INVALID_ARGUMENT
+    # disarming with nothing armed is a no-op
+    _native.kernel_timer_arm((), 0)
+    n = ctypes.c_int32(-1)
+    assert lib.nnue_ft_kernel_timer_read(3, None, 0, ctypes.byref(n)) == _native.NNUE_ERR_INVALID_ARGUMENT
+    assert _native.kernel_timer_read(_native.TIMED_LIGHT_ROWS) == []

@@ -45,6 +45,7 @@ extern "C" {
 #define NNUE_DEVERR_BAD_QUANT_INDEX 2u   /* quantised forward: index outside the table */
 #define NNUE_DEVERR_BAD_SEGMENT 4u       /* backward: corrupt workspace (position out of range) */
 #define NNUE_DEVERR_BAD_PSQT_INDEX 8u    /* epilogue: PSQT bucket index outside [0, n_psqt) was skipped */
+#define NNUE_DEVERR_BAD_POSITION 16u     /* device encoder: a rejected position got all -1 rows */
 
 /* ABI version (major * 100 + minor). */
 int nnue_ft_version(void);
@@ -311,9 +312,25 @@ int nnue_generate_positions(uint64_t seed, int64_t first, int64_t count, uint8_t
  * (src/rust/feature_extraction.rs:213-241, 391-404, 581-739):
  * feature_set 0 = HalfKAv2_hm (K = 32), 1 = Full_Threats (K = 128),
  * 2 = Full_Threats+HalfKAv2_hm (K = 160).  white/black: [count, K] int32,
- * compacted, -1 padded; counts (nullable): [count] each.  Host memory. */
+ * compacted, -1 padded; counts (nullable): [count] each.  Host memory.
+ * Returns NNUE_ERR_INVALID_ARGUMENT (the rejected positions' rows all -1)
+ * when a position has a side without a king, a pawn on the first or last
+ * rank, or more than 128 threat / 32 HalfKA features. */
 int nnue_encode_features(const uint8_t *board, int64_t count, int32_t feature_set, int32_t *white,
                          int32_t *black, int32_t *white_count, int32_t *black_count, int32_t nthreads);
+
+/* The same feature indices as nnue_encode_features, computed on the GPU
+ * from boards in DEVICE memory (replaces the reference's host-side encoder,
+ * src/rust/feature_extraction.rs:213-241 via fill_feature_indices_sparse,
+ * for a loader that ships boards -- 64 bytes per position -- instead of
+ * index rows of 4 * K bytes per perspective).  board: [count, 64] uint8;
+ * white/black: [count, K] int32 (K = 32, 128, 160 for feature_set 0, 1, 2),
+ * compacted and -1 padded; counts (nullable): [count] int32.  A position the
+ * host encoder rejects (a side without a king, a pawn on the first or last
+ * rank, more than 128 threat or 32 HalfKA features) gets all -1 rows and
+ * count 0 and raises NNUE_DEVERR_BAD_POSITION.  Async on `stream`. */
+int nnue_ft_encode_features(const uint8_t *board, int64_t count, int32_t feature_set, int32_t *white,
+                            int32_t *black, int32_t *white_count, int32_t *black_count, void *stream);
 
 #ifdef __cplusplus
 }

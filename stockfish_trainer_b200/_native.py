@@ -28,6 +28,7 @@ NNUE_ERR_CUDA = -4
 DEVERR_BAD_INDEX = 1
 DEVERR_BAD_QUANT_INDEX = 2
 DEVERR_BAD_PSQT_INDEX = 8
+DEVERR_BAD_POSITION = 16
 
 _SIGNATURES = {
     "nnue_ft_version": (_I32, []),
@@ -65,6 +66,7 @@ _SIGNATURES = {
     "nnue_threat_table_total": (_I32, []),
     "nnue_generate_positions": (_I32, [_U64, _I64, _I64, _P, _P]),
     "nnue_encode_features": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _I32]),
+    "nnue_ft_encode_features": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

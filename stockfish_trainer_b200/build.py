@@ -24,7 +24,8 @@ LIB_NAME = "libnnue_ft.so"
 LIB_PATH = os.path.join(PKG, LIB_NAME)
 
 SOURCES = ["nnue_ft.cu", "features.cpp"]
-DEPS = SOURCES + ["common.cuh", "ft_forward.cuh", "ft_backward.cuh", "ft_quant.cuh"]
+DEPS = SOURCES + ["common.cuh", "ft_forward.cuh", "ft_backward.cuh", "ft_quant.cuh", "ft_epilogue.cuh",
+                  "ft_optim.cuh", "ft_encode.cuh", "feature_tables.h", "feature_encode.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

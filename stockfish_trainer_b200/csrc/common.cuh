@@ -21,6 +21,7 @@ enum : unsigned {
   kErrBadQuantIndex = 2u,  // quantised forward: index outside the table / export map
   kErrBadSegment = 4u,     // backward: a sorted position outside [0, batch) (corrupt workspace)
   kErrBadPsqtIndex = 8u,   // epilogue: PSQT bucket index outside [0, n_psqt)
+  kErrBadPosition = 16u,   // encoder: a position the feature functions reject (its rows are all -1)
 };
 
 __device__ __forceinline__ void flag_error(unsigned e) { atomicOr(&g_device_errors, e); }

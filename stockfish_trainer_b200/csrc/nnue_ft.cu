@@ -22,6 +22,7 @@
 #include "ft_epilogue.cuh"
 #include "ft_optim.cuh"
 #include "ft_quant.cuh"
+#include "ft_encode.cuh"
 
 namespace nnue {
 namespace {
@@ -564,6 +565,30 @@ int launch_segsum_heavy(SegParams p, cudaStream_t s) {
   return NNUE_OK;
 }
 
+// Per-device copy of the encoder's lookup tables, made on first use.
+std::mutex g_enc_mu;
+nnue_feat::FeatureTables* g_enc_tables[64] = {};
+
+int encoder_tables(const nnue_feat::FeatureTables** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("encode_features: device");
+  if (dev < 0 || dev >= 64) return fail(NNUE_ERR_UNSUPPORTED, "encode_features: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_enc_mu);
+  if (!g_enc_tables[dev]) {
+    nnue_feat::FeatureTables* d = nullptr;
+    if (cudaMalloc(&d, sizeof(nnue_feat::FeatureTables)) != cudaSuccess)
+      return check_launch("encode_features: table allocation");
+    if (cudaMemcpy(d, &nnue_feat::feature_tables(), sizeof(nnue_feat::FeatureTables), cudaMemcpyHostToDevice) !=
+        cudaSuccess) {
+      cudaFree(d);
+      return check_launch("encode_features: table upload");
+    }
+    g_enc_tables[dev] = d;
+  }
+  *out = g_enc_tables[dev];
+  return NNUE_OK;
+}
+
 // Per-device side stream + fork/join events.  Heavy rows and the bias column
 // sum run there, concurrently with the light-row kernel on the caller's
 // stream.  Created once per device and kept for the life of the process.
@@ -809,6 +834,37 @@ extern "C" {
 int nnue_ft_version(void) { return 100; }
 
 uint64_t nnue_ft_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int nnue_ft_encode_features(const uint8_t* board, int64_t count, int32_t feature_set, int32_t* white,
+                            int32_t* black, int32_t* white_count, int32_t* black_count, void* stream) {
+  if (feature_set < 0 || feature_set > 2 || count < 0)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "encode_features: feature_set %d, count %lld", (int)feature_set,
+                (long long)count);
+  if (count == 0) return NNUE_OK;
+  if (!board || !white || !black) return fail(NNUE_ERR_INVALID_ARGUMENT, "encode_features: null pointer");
+  if (count > (int64_t)INT32_MAX * kEncPositions)
+    return fail(NNUE_ERR_UNSUPPORTED, "encode_features: %lld positions", (long long)count);
+  const nnue_feat::FeatureTables* tables = nullptr;
+  int rc = encoder_tables(&tables);
+  if (rc != NNUE_OK) return rc;
+  EncParams p{};
+  p.board = board;
+  p.count = count;
+  p.feature_set = feature_set;
+  p.K = feature_set == 0 ? nnue_feat::kHalfkaMax
+        : feature_set == 1 ? nnue_feat::kThreatMax
+                           : nnue_feat::kThreatMax + nnue_feat::kHalfkaMax;
+  p.board_vec16 = aligned16(board) ? 1 : 0;
+  p.out[0] = white;
+  p.out[1] = black;
+  p.counts[0] = white_count;
+  p.counts[1] = black_count;
+  p.tables = tables;
+  count_launch();
+  encode_features_kernel<<<(unsigned)ceil_div(count, kEncPositions), kEncThreads, 0,
+                           static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("encode_features");
+}
 
 int nnue_ft_kernel_timer_arm(uint32_t kernels, int32_t capacity) {
   if (kernels >= (1u << kTimedKinds) || capacity < 0 || (kernels && capacity == 0))

@@ -60,6 +60,32 @@ def encode(board: np.ndarray, feature_set: str, nthreads: int = 0):
     return white, black, wc, bc
 
 
+def encode_device(board, feature_set: str, with_counts: bool = False):
+    """The same index rows as ``encode``, computed on the GPU from a uint8
+    ``[n, 64]`` board tensor in device memory (nnue_ft_encode_features):
+    returns white and black ``[n, K]`` int32 device tensors (+ counts).  A
+    loader can ship boards (64 bytes per position) instead of index rows
+    (4 * K bytes per perspective).  Rejected positions get all -1 rows and
+    raise the device error flag DEVERR_BAD_POSITION."""
+    import torch
+
+    fid, _, K = feature_set_info(feature_set)
+    if board.dtype != torch.uint8 or board.dim() != 2 or board.shape[1] != 64 or not board.is_contiguous():
+        raise ValueError("board must be a contiguous [n, 64] uint8 tensor")
+    if not board.is_cuda:
+        raise ValueError("encode_device needs a CUDA tensor")
+    n, dev = board.shape[0], board.device
+    white = torch.empty(n, K, dtype=torch.int32, device=dev)
+    black = torch.empty(n, K, dtype=torch.int32, device=dev)
+    wc = torch.empty(n, dtype=torch.int32, device=dev) if with_counts else None
+    bc = torch.empty(n, dtype=torch.int32, device=dev) if with_counts else None
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _native.call("nnue_ft_encode_features", board.data_ptr(), n, fid, white.data_ptr(), black.data_ptr(),
+                     wc.data_ptr() if wc is not None else None, bc.data_ptr() if bc is not None else None, stream)
+    return (white, black, wc, bc) if with_counts else (white, black)
+
+
 def synthetic_batch(n: int, feature_set: str, seed: int = 0, first: int = 0):
     """(white [n, K], black [n, K], side to move [n]) for n seeded positions."""
     board, stm = generate_positions(n, seed, first)

@@ -103,3 +103,28 @@ def test_encode_rejects_position_without_king():
     board = np.full((1, 64), 12, np.uint8)
     with pytest.raises(RuntimeError):
         P.encode(board, "HalfKAv2_hm^")
+
+
+def test_host_encoder_rejects_invalid_positions():
+    """A perspective without its king, or any pawn on a back rank (the
+    reference's threat table has no slot for such pawns), is rejected: the
+    batch reports INVALID_ARGUMENT and the rejected rows are all -1, the
+    others intact."""
+    from stockfish_trainer_b200 import _native
+
+    boards = np.array([F.parse_fen(f)[0] for f in REFERENCE_FENS], np.uint8)
+    bad = boards.copy()
+    bad[1][bad[1] == 11] = 12          # position 1: no black king
+    bad[2][60] = 0                     # position 2: a white pawn on e8
+    good_w, good_b, _, _ = P.encode(boards, "Full_Threats+HalfKAv2_hm^")
+    with pytest.raises(_native.NativeError):
+        P.encode(bad, "Full_Threats+HalfKAv2_hm^")
+    K = 160
+    w = np.empty((4, K), np.int32)
+    b = np.empty((4, K), np.int32)
+    rc = _native.load().nnue_encode_features(bad.ctypes.data, 4, 2, w.ctypes.data, b.ctypes.data, None, None, 0)
+    assert rc == _native.NNUE_ERR_INVALID_ARGUMENT
+    assert np.all(b[1] == -1) and (w[1] >= 0).sum() > 0  # only black lacks its king
+    assert np.all(w[2] == -1) and np.all(b[2] == -1)
+    np.testing.assert_array_equal(w[[0, 3]], good_w[[0, 3]])
+    np.testing.assert_array_equal(b[[0, 3]], good_b[[0, 3]])

@@ -572,12 +572,89 @@ def run_ours(args):
         e3.record()
         barrier()
         ms_serial = max_over_ranks(s3.elapsed_time(e3)) / args.steps
+
+        # Boards instead of index rows: the loader ships 64 bytes per position
+        # (copied on the copy stream one step ahead, double-buffered) and the
+        # device encoder (nnue_ft_encode_features, bit-identical to the host
+        # encoder) builds both perspectives' index rows at the start of the
+        # step.  (Encoding one step ahead on the copy stream instead measured
+        # slower: its blocks take SM room the forward's gathers need.)
+        board_np, _ = positions.generate_positions(b_rank, seed=args.seed, first=first)  # the same positions
+        hboard = torch.from_numpy(board_np).pin_memory()
+        bbuf = [torch.empty(b_rank, 64, dtype=torch.uint8, device=dev) for _ in range(2)]
+        ibuf = (torch.empty_like(i0), torch.empty_like(i1))
+        bcopied = [torch.cuda.Event() for _ in range(2)]
+        bconsumed = [torch.cuda.Event() for _ in range(2)]
+
+        def enqueue_board_copy(k):
+            s = k % 2
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(bconsumed[s])
+                bbuf[s].copy_(hboard, non_blocking=True)
+                bcopied[s].record(copy_stream)
+
+        def boards_step(k):
+            s = k % 2
+            cur = torch.cuda.current_stream(dev)
+            cur.wait_event(bcopied[s])
+            enqueue_board_copy(k + 1)
+            positions.encode_device(bbuf[s], args.feature_set, out=ibuf)
+            bconsumed[s].record(cur)
+            o0, o1 = SparseLinearPairFunction.apply(ibuf[0], ibuf[1], Wp, bp)
+            torch.autograd.backward([o0, o1], [g0, g1])
+            if world > 1:
+                dist.all_reduce(Wp.grad)
+                dist.all_reduce(bp.grad)
+                Wp.grad.div_(world)
+                bp.grad.div_(world)
+            host_out.copy_(bp.grad, non_blocking=True)
+            Wp.grad = None
+            bp.grad = None
+
+        enqueue_board_copy(0)
+        for k in range(n_warm):
+            boards_step(k)
+        barrier()
+        s4, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s4.record()
+        for k in range(n_warm, n_warm + args.steps):
+            boards_step(k)
+        e4.record()
+        barrier()
+        ms_boards = max_over_ranks(s4.elapsed_time(e4)) / args.steps
+        # the device encoder alone, boards resident
+        s5, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s5.record()
+        for _ in range(args.steps):
+            positions.encode_device(bbuf[0], args.feature_set)
+        e5.record()
+        barrier()
+        ms_encode = max_over_ranks(s5.elapsed_time(e5)) / args.steps
+        if _native.device_errors(clear=True):
+            raise RuntimeError("device encoder rejected a synthetic position")
+        host_enc = None
+        if rank == 0:
+            sample = board_np[: min(b_rank, 16384)]
+            positions.encode(sample, args.feature_set)
+            t0 = time.perf_counter()
+            positions.encode(sample, args.feature_set)
+            host_enc = sample.shape[0] / (time.perf_counter() - t0)
         e2e = {"value": args.batch / (ms_e2e / 1e3), "unit": "positions/s",
                "h2d_bytes_per_step": int(h0.numel() * 4 + h1.numel() * 4), "d2h_bytes_per_step": C * 4,
                "ms_per_step": ms_e2e,
                "path": "SparseLinearPairFunction autograd fwd+bwd; each step's indices copied from pinned "
                        "host memory on a copy stream one step ahead (double-buffered); bias grad read back",
-               "serial_copy_ms_per_step": ms_serial}
+               "serial_copy_ms_per_step": ms_serial,
+               "boards": {"value": args.batch / (ms_boards / 1e3), "unit": "positions/s",
+                          "ms_per_step": ms_boards, "h2d_bytes_per_step": int(hboard.numel()),
+                          "d2h_bytes_per_step": C * 4,
+                          "path": "boards [B, 64] uint8 copied from pinned host memory on a copy stream one "
+                                  "step ahead (double-buffered), encoded on the device at the start of the "
+                                  "step (nnue_ft_encode_features), then the same autograd step",
+                          "device_encode_ms": ms_encode,
+                          "device_encode_positions_per_s": b_rank / (ms_encode / 1e3),
+                          "host_encoder_positions_per_s": host_enc,
+                          "host_encoder_threads": os.cpu_count()}}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -15,10 +15,8 @@
 
 #if defined(__CUDACC__)
 #define NNUE_HD __host__ __device__ __forceinline__
-#define NNUE_UNROLL _Pragma("unroll")
 #else
 #define NNUE_HD inline
-#define NNUE_UNROLL
 #endif
 
 namespace nnue_feat {
@@ -100,21 +98,31 @@ NNUE_HD bool pawns_on_valid_ranks(const PosView& p) {
   return ((p.by_piece[kPawn * 2 + kWhite] | p.by_piece[kPawn * 2 + kBlack]) & back_ranks) == 0;
 }
 
-// fill_halfka_feature_indices_sparse: occupied squares ascending.
-// Returns the count, or -1 (no king of that colour) or -2 (more than
-// kHalfkaMax pieces).
-NNUE_HD int encode_halfka(const FeatureTables& t, const PosView& p, int color, int32_t* out) {
+// Output sinks take the indices in order.  RowSink writes them straight into
+// a row; the device encoder uses a buffering sink (ft_encode.cuh).
+struct RowSink {
+  int32_t* row;
+  int n;
+  NNUE_HD void push(int v) { row[n++] = v; }
+};
+
+// fill_halfka_feature_indices_sparse: occupied squares ascending, each index
+// plus `offset`.  Returns the count, or -1 (no king of that colour) or -2
+// (more than kHalfkaMax pieces).
+template <class Sink>
+NNUE_HD int encode_halfka(const FeatureTables& t, const PosView& p, int color, int offset, Sink& out) {
   const int ksq = king_sq(p, color);
   if (ksq < 0) return -1;
   if (popcount64(p.occ) > kHalfkaMax) return -2;
   const int m = halfka_orient(color, ksq);
-  const int bucket = t.king_bucket[ksq ^ m];
+  const int base = t.king_bucket[ksq ^ m] * 768 + offset;
   int n = 0;
   for (uint64_t occ = p.occ; occ; occ &= occ - 1) {
     const int sq = lsb64(occ);
     const int id = p.board[sq];
     const int piece_index = (id >> 1) * 2 + ((id & 1) != color);
-    out[n++] = (sq ^ m) + piece_index * 64 + bucket * 768;
+    out.push((sq ^ m) + piece_index * 64 + base);
+    ++n;
   }
   return n;
 }
@@ -150,41 +158,41 @@ NNUE_HD int threat_index(const FeatureTables& t, int persp, int attacker, int fr
 // pawns as left captures, right captures, pushes onto pawns; other pieces
 // by origin square, targets ascending.  Returns the count, or -1 (no king /
 // a pawn on a back rank) or -2 (more than `cap` features).
-NNUE_HD int encode_threats(const FeatureTables& t, const PosView& p, int persp, int32_t* out, int cap) {
+template <class Sink>
+NNUE_HD int encode_threats(const FeatureTables& t, const PosView& p, int persp, Sink& out, int cap) {
   const int ksq = king_sq(p, persp);
   if (ksq < 0 || !pawns_on_valid_ranks(p)) return -1;
   const uint64_t kAFile = 0x0101010101010101ull, kHFile = 0x8080808080808080ull;
   const uint64_t pawns = p.by_piece[kPawn * 2 + kWhite] | p.by_piece[kPawn * 2 + kBlack];
   int n = 0;
+  int attacker = 0;
+  // one feature per pawn target in `set`; false when the row overflows
+  auto pawn_set = [&](uint64_t set, int delta) -> bool {
+    for (uint64_t x = set; x; x &= x - 1) {
+      const int to = lsb64(x);
+      const int idx = threat_index(t, persp, attacker, to + delta, to, p.board[to], ksq);
+      if (idx >= 0) {
+        if (n >= cap) return false;
+        out.push(idx);
+        ++n;
+      }
+    }
+    return true;
+  };
   for (int ci = 0; ci < 2; ++ci) {
     const int color = ci == 0 ? persp : 1 - persp;
     for (int pt = 0; pt < 6; ++pt) {
-      const int attacker = pt * 2 + color;
+      attacker = pt * 2 + color;
       const uint64_t bb = p.by_piece[attacker];
       if (pt == kPawn) {
-        uint64_t sets[3];
-        int delta[3];
-        if (color == kWhite) {
-          sets[0] = ((bb & ~kHFile) << 9) & p.occ;
-          sets[1] = ((bb & ~kAFile) << 7) & p.occ;
-          sets[2] = (bb << 8) & pawns;
-          delta[0] = -9, delta[1] = -7, delta[2] = -8;
-        } else {
-          sets[0] = ((bb & ~kAFile) >> 9) & p.occ;
-          sets[1] = ((bb & ~kHFile) >> 7) & p.occ;
-          sets[2] = (bb >> 8) & pawns;
-          delta[0] = 9, delta[1] = 7, delta[2] = 8;
-        }
-        NNUE_UNROLL
-        for (int s = 0; s < 3; ++s)
-          for (uint64_t x = sets[s]; x; x &= x - 1) {
-            const int to = lsb64(x);
-            const int idx = threat_index(t, persp, attacker, to + delta[s], to, p.board[to], ksq);
-            if (idx >= 0) {
-              if (n >= cap) return -2;
-              out[n++] = idx;
-            }
-          }
+        // left captures, right captures, pushes onto pawns; `delta` maps a
+        // target square back to the pawn's square
+        const bool white = color == kWhite;
+        const uint64_t left = (white ? (bb & ~kHFile) << 9 : (bb & ~kAFile) >> 9) & p.occ;
+        const uint64_t right = (white ? (bb & ~kAFile) << 7 : (bb & ~kHFile) >> 7) & p.occ;
+        const uint64_t push = (white ? bb << 8 : bb >> 8) & pawns;
+        if (!pawn_set(left, white ? -9 : 9) || !pawn_set(right, white ? -7 : 7) || !pawn_set(push, white ? -8 : 8))
+          return -2;
       } else {
         for (uint64_t f = bb; f; f &= f - 1) {
           const int from = lsb64(f);
@@ -193,7 +201,8 @@ NNUE_HD int encode_threats(const FeatureTables& t, const PosView& p, int persp, 
             const int idx = threat_index(t, persp, attacker, from, to, p.board[to], ksq);
             if (idx >= 0) {
               if (n >= cap) return -2;
-              out[n++] = idx;
+              out.push(idx);
+              ++n;
             }
           }
         }
@@ -206,8 +215,10 @@ NNUE_HD int encode_threats(const FeatureTables& t, const PosView& p, int persp, 
 // FeatureSet::fill_feature_indices_sparse: components in order (threats,
 // then HalfKA offset by the threat inputs), compacted; the caller fills the
 // -1 tail.  feature_set 0 = HalfKAv2_hm, 1 = Full_Threats, 2 = both.
-// Returns the count or a negative status (the position is rejected).
-NNUE_HD int encode_position(const FeatureTables& t, const PosView& p, int color, int feature_set, int32_t* out) {
+// Returns the count or a negative status (the position is rejected; the
+// sink may hold a partial row).
+template <class Sink>
+NNUE_HD int encode_position(const FeatureTables& t, const PosView& p, int color, int feature_set, Sink& out) {
   int n = 0;
   if (feature_set == 1 || feature_set == 2) {
     const int c = encode_threats(t, p, color, out, kThreatMax);
@@ -215,10 +226,8 @@ NNUE_HD int encode_position(const FeatureTables& t, const PosView& p, int color,
     n = c;
   }
   if (feature_set == 0 || feature_set == 2) {
-    const int offset = feature_set == 2 ? kThreatInputs : 0;
-    const int c = encode_halfka(t, p, color, out + n);
+    const int c = encode_halfka(t, p, color, feature_set == 2 ? kThreatInputs : 0, out);
     if (c < 0) return c;
-    for (int i = 0; i < c; ++i) out[n + i] += offset;
     n += c;
   }
   return n;

@@ -192,8 +192,9 @@ int nnue_generate_positions(uint64_t seed, int64_t first, int64_t count, uint8_t
         Pos p;
         load(bd, p);
         const FeatureTables& t = feature_tables();
-        if (encode_threats(t, p.view(), kWhite, scratch, kThreatMax) >= 0 &&
-            encode_threats(t, p.view(), kBlack, scratch, kThreatMax) >= 0)
+        RowSink sw{scratch, 0}, sb{scratch, 0};
+        if (encode_threats(t, p.view(), kWhite, sw, kThreatMax) >= 0 &&
+            encode_threats(t, p.view(), kBlack, sb, kThreatMax) >= 0)
           break;
       }
     }
@@ -215,7 +216,8 @@ int nnue_encode_features(const uint8_t* board, int64_t count, int32_t feature_se
       int32_t* rows[2] = {white + i * K, black + i * K};
       int32_t* counts[2] = {white_count, black_count};
       for (int c = 0; c < 2; ++c) {
-        const int n = encode_position(feature_tables(), p.view(), c, feature_set, rows[c]);
+        RowSink sink{rows[c], 0};
+        const int n = encode_position(feature_tables(), p.view(), c, feature_set, sink);
         if (n < 0) {
           status[i] = n;
           std::fill(rows[c], rows[c] + K, -1);

@@ -30,6 +30,37 @@ struct EncParams {
 constexpr int kEncThreads = 128;
 constexpr int kEncPositions = kEncThreads / 2;
 
+// Buffers four indices and writes them as one 16-byte store: a warp's 32
+// rows are 32 different rows, so 4-byte stores would cost one L2 request
+// per index.  Rows must be 16-byte aligned with K % 4 == 0.
+struct Int4Sink {
+  int32_t* row;
+  int n;
+  int4 buf;
+  __device__ __forceinline__ void push(int v) {
+    const int r = n & 3;
+    buf.x = r == 0 ? v : buf.x;
+    buf.y = r == 1 ? v : buf.y;
+    buf.z = r == 2 ? v : buf.z;
+    buf.w = r == 3 ? v : buf.w;
+    ++n;
+    if (r == 3) reinterpret_cast<int4*>(row)[(n >> 2) - 1] = buf;
+  }
+  // the -1 tail from n up to K
+  __device__ __forceinline__ void finish(int K) {
+    int q = n >> 2;
+    const int r = n & 3;
+    if (r) {
+      if (r <= 1) buf.y = -1;
+      if (r <= 2) buf.z = -1;
+      buf.w = -1;
+      reinterpret_cast<int4*>(row)[q++] = buf;
+    }
+    for (; q < (K >> 2); ++q) reinterpret_cast<int4*>(row)[q] = make_int4(-1, -1, -1, -1);
+  }
+};
+
+template <bool kVec>
 __global__ void __launch_bounds__(kEncThreads) encode_features_kernel(const EncParams p) {
   __shared__ nnue_feat::FeatureTables t;
   __shared__ __align__(16) uint8_t boards[kEncPositions][64];
@@ -74,12 +105,21 @@ __global__ void __launch_bounds__(kEncThreads) encode_features_kernel(const EncP
   const int64_t pos = pos0 + li;
   const nnue_feat::PosView v{bbs[li], bbs[li][12], boards[li]};
   int32_t* row = p.out[persp] + pos * p.K;
-  int n = nnue_feat::encode_position(t, v, persp, p.feature_set, row);
+  int n;
+  if constexpr (kVec) {
+    Int4Sink sink{row, 0, make_int4(-1, -1, -1, -1)};
+    n = nnue_feat::encode_position(t, v, persp, p.feature_set, sink);
+    if (n < 0) sink.n = 0;  // rejected: the whole row becomes -1
+    sink.finish(p.K);
+  } else {
+    nnue_feat::RowSink sink{row, 0};
+    n = nnue_feat::encode_position(t, v, persp, p.feature_set, sink);
+    for (int i = n < 0 ? 0 : n; i < p.K; ++i) row[i] = -1;
+  }
   if (n < 0) {  // rejected position: an all -1 row, reported
     flag_error(kErrBadPosition);
     n = 0;
   }
-  for (int i = n; i < p.K; ++i) row[i] = -1;
   if (p.counts[persp]) p.counts[persp][pos] = n;
 }
 

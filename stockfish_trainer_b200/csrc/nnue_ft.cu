@@ -861,8 +861,11 @@ int nnue_ft_encode_features(const uint8_t* board, int64_t count, int32_t feature
   p.counts[1] = black_count;
   p.tables = tables;
   count_launch();
-  encode_features_kernel<<<(unsigned)ceil_div(count, kEncPositions), kEncThreads, 0,
-                           static_cast<cudaStream_t>(stream)>>>(p);
+  const unsigned grid = (unsigned)ceil_div(count, kEncPositions);
+  if (aligned16(white) && aligned16(black))  // rows are 16-byte multiples (K % 4 == 0)
+    encode_features_kernel<true><<<grid, kEncThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  else
+    encode_features_kernel<false><<<grid, kEncThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("encode_features");
 }
 

@@ -60,10 +60,11 @@ def encode(board: np.ndarray, feature_set: str, nthreads: int = 0):
     return white, black, wc, bc
 
 
-def encode_device(board, feature_set: str, with_counts: bool = False):
+def encode_device(board, feature_set: str, with_counts: bool = False, out=None):
     """The same index rows as ``encode``, computed on the GPU from a uint8
-    ``[n, 64]`` board tensor in device memory (nnue_ft_encode_features):
-    returns white and black ``[n, K]`` int32 device tensors (+ counts).  A
+    ``[n, 64]`` board tensor in device memory (nnue_ft_encode_features), on
+    the current stream: returns white and black ``[n, K]`` int32 device
+    tensors (+ counts), written into ``out = (white, black)`` when given.  A
     loader can ship boards (64 bytes per position) instead of index rows
     (4 * K bytes per perspective).  Rejected positions get all -1 rows and
     raise the device error flag DEVERR_BAD_POSITION."""
@@ -75,8 +76,14 @@ def encode_device(board, feature_set: str, with_counts: bool = False):
     if not board.is_cuda:
         raise ValueError("encode_device needs a CUDA tensor")
     n, dev = board.shape[0], board.device
-    white = torch.empty(n, K, dtype=torch.int32, device=dev)
-    black = torch.empty(n, K, dtype=torch.int32, device=dev)
+    if out is not None:
+        white, black = out
+        for t in (white, black):
+            if t.dtype != torch.int32 or tuple(t.shape) != (n, K) or not t.is_contiguous() or t.device != dev:
+                raise ValueError(f"out tensors must be contiguous [{n}, {K}] int32 on {dev}")
+    else:
+        white = torch.empty(n, K, dtype=torch.int32, device=dev)
+        black = torch.empty(n, K, dtype=torch.int32, device=dev)
     wc = torch.empty(n, dtype=torch.int32, device=dev) if with_counts else None
     bc = torch.empty(n, dtype=torch.int32, device=dev) if with_counts else None
     with torch.cuda.device(dev):

@@ -79,10 +79,11 @@ int nnue_ft_device_errors(uint32_t *flags, int clear);
 
 /* Tuning knobs (names: "fwd_chunk_vec", "fwd_items_per_warp", "fwd_unroll",
  * "fwd_min_blocks", "fwd_exact_chunks", "bwd_chunk_vec", "bwd_unroll",
- * "bwd_min_blocks", "bwd_exact_chunks", "bwd_variant", "bwd_stream_cfg",
- * "bwd_entries_per_warp", "heavy_threshold", "heavy_cap", "sort_tile_rows",
- * "sort_tile", "colsum_parts"); unknown names and out-of-range values are
- * rejected with NNUE_ERR_INVALID_ARGUMENT.
+ * "bwd_min_blocks", "bwd_exact_chunks", "bwd_block", "bwd_variant",
+ * "bwd_stream_cfg", "bwd_entries_per_warp", "heavy_threshold", "heavy_cap",
+ * "sort_variant", "sort_blocks_per_sm", "sort_tile_rows", "sort_tile",
+ * "colsum_parts"); unknown names and out-of-range values are rejected with
+ * NNUE_ERR_INVALID_ARGUMENT.  Every setting gives the same results.
  * Process-wide; change them only while no call is in flight and never between
  * a backward_prepare and its backward_apply. */
 int nnue_ft_set_param(const char *name, int64_t value);
@@ -328,7 +329,9 @@ int nnue_encode_features(const uint8_t *board, int64_t count, int32_t feature_se
  * compacted and -1 padded; counts (nullable): [count] int32.  A position the
  * host encoder rejects (a side without a king, a pawn on the first or last
  * rank, more than 128 threat or 32 HalfKA features) gets all -1 rows and
- * count 0 and raises NNUE_DEVERR_BAD_POSITION.  Async on `stream`. */
+ * count 0 and raises NNUE_DEVERR_BAD_POSITION.  Async on `stream`, except
+ * the first call on a device, which uploads the encoder's lookup tables
+ * (13 KB, into a static device array) synchronously. */
 int nnue_ft_encode_features(const uint8_t *board, int64_t count, int32_t feature_set, int32_t *white,
                             int32_t *black, int32_t *white_count, int32_t *black_count, void *stream);
 

@@ -743,15 +743,15 @@ __device__ __forceinline__ void seg_sum(VT (&acc)[V], const VT* __restrict__ src
 // x one 512-byte row slice, so MINB (resident blocks the register budget is
 // sized for) matters as much as U.  Heavy rows are left to
 // ft_segsum_heavy_kernel.
-template <typename VT, int V, int U, int MINB = 1>
-__global__ void __launch_bounds__(kBlock, MINB) ft_segsum_light_kernel(const SegParams p) {
+template <typename VT, int V, int U, int MINB = 1, int BLOCK = kBlock>
+__global__ void __launch_bounds__(BLOCK, MINB) ft_segsum_light_kernel(const SegParams p) {
   using Ops = Vec<VT>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunk = p.chunk0 + blockIdx.y;
   const int c0 = p.g.begin(chunk);
   const int width = p.g.width(chunk);
   const int row_vec = p.g.n_vec;
-  const int64_t f = p.row_begin + (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  const int64_t f = p.row_begin + (int64_t)blockIdx.x * (BLOCK / 32) + warp;
   if (f >= p.row_end) return;
   const int P = p.P;
   const int bnd = lane <= P ? p.seg_start[f * P + lane] : 0;

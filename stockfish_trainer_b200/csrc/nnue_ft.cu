@@ -108,6 +108,7 @@ struct Tuning {
   int64_t sort_variant = 1;        // 1: counting placement + per-segment sort, 0: LSD radix passes
   int64_t sort_blocks_per_sm = 16;  // counting placement: grid of the two passes over the index arrays
   int64_t colsum_parts = 296;      // position ranges of the bias column sum
+  int64_t bwd_block = 128;         // light rows: threads per block (256, 128 or 64; 1 vector per lane, 2-row batches)
 };
 Tuning g_tune;
 
@@ -138,6 +139,7 @@ ParamRef* params() {
       {"sort_blocks_per_sm", &g_tune.sort_blocks_per_sm, 1, 1 << 16},
       {"sort_tile", &g_tune.sort_tile, 32 * kSortBatch, 1 << 20},
       {"colsum_parts", &g_tune.colsum_parts, 1, 1 << 16},
+      {"bwd_block", &g_tune.bwd_block, 64, 256},
       {nullptr, nullptr, 0, 0},
   };
   return p;
@@ -498,6 +500,20 @@ void launch_segsum_vu(SegParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(p.row_end - p.row_begin, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
+  if constexpr (V == 1 && U == 2) {
+    // smaller blocks: a block's warp slots are released only when its
+    // longest row is done, and light rows differ widely in length
+    const int64_t rows = p.row_end - p.row_begin;
+    if (g_tune.bwd_block == 64 && g_tune.bwd_min_blocks == 8) {
+      ft_segsum_light_kernel<VT, 1, 2, 32, 64><<<dim3((unsigned)ceil_div(rows, 2), (unsigned)n_chunks), 64, 0, s>>>(p);
+      return;
+    }
+    if (g_tune.bwd_block == 128 && g_tune.bwd_min_blocks == 8) {
+      ft_segsum_light_kernel<VT, 1, 2, 16, 128><<<dim3((unsigned)ceil_div(rows, 4), (unsigned)n_chunks), 128, 0, s>>>(
+          p);
+      return;
+    }
+  }
   if constexpr (V <= 2) {
     // two vectors per lane need twice the registers: cap their budget at 4 blocks
     switch (V == 1 ? g_tune.bwd_min_blocks : std::min<int64_t>(g_tune.bwd_min_blocks, 4)) {
@@ -565,9 +581,12 @@ int launch_segsum_heavy(SegParams p, cudaStream_t s) {
   return NNUE_OK;
 }
 
-// Per-device copy of the encoder's lookup tables, made on first use.
+// The encoder's lookup tables live in a static device array (no device
+// allocation); each device gets its copy on its first encoder call, a
+// synchronous upload.
+__device__ nnue_feat::FeatureTables g_enc_tables_dev;
 std::mutex g_enc_mu;
-nnue_feat::FeatureTables* g_enc_tables[64] = {};
+const nnue_feat::FeatureTables* g_enc_tables[64] = {};
 
 int encoder_tables(const nnue_feat::FeatureTables** out) {
   int dev = 0;
@@ -575,15 +594,12 @@ int encoder_tables(const nnue_feat::FeatureTables** out) {
   if (dev < 0 || dev >= 64) return fail(NNUE_ERR_UNSUPPORTED, "encode_features: device %d", dev);
   std::lock_guard<std::mutex> lock(g_enc_mu);
   if (!g_enc_tables[dev]) {
-    nnue_feat::FeatureTables* d = nullptr;
-    if (cudaMalloc(&d, sizeof(nnue_feat::FeatureTables)) != cudaSuccess)
-      return check_launch("encode_features: table allocation");
-    if (cudaMemcpy(d, &nnue_feat::feature_tables(), sizeof(nnue_feat::FeatureTables), cudaMemcpyHostToDevice) !=
-        cudaSuccess) {
-      cudaFree(d);
+    void* d = nullptr;
+    if (cudaMemcpyToSymbol(g_enc_tables_dev, &nnue_feat::feature_tables(), sizeof(nnue_feat::FeatureTables)) !=
+            cudaSuccess ||
+        cudaGetSymbolAddress(&d, g_enc_tables_dev) != cudaSuccess)
       return check_launch("encode_features: table upload");
-    }
-    g_enc_tables[dev] = d;
+    g_enc_tables[dev] = static_cast<const nnue_feat::FeatureTables*>(d);
   }
   *out = g_enc_tables[dev];
   return NNUE_OK;

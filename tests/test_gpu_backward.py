@@ -115,6 +115,9 @@ def _with_params(params, fn):
         {"bwd_unroll": 8, "bwd_min_blocks": 4},
         {"bwd_unroll": 4, "bwd_min_blocks": 0},
         {"bwd_unroll": 4, "bwd_min_blocks": 5, "bwd_chunk_vec": 64, "bwd_exact_chunks": 1},
+        {"bwd_block": 256},
+        {"bwd_block": 128},
+        {"bwd_block": 64},
     ],
 )
 def test_backward_tuning_and_heavy_rows(cuda, params):

@@ -48,8 +48,8 @@ C = L1 + NPSQT
 # gather kernels in the default 1-GPU headline run, from a one-pass ncu
 # capture of that command (profiles/dram_traffic_headline_fullsize.md).
 TRAFFIC_HEADLINE: dict = {
-    "ft_forward_kernel": 1.7705e9 + 0.5321e9,
-    "ft_segsum_light_kernel": 1.7176e9 + 0.3473e9,
+    "ft_forward_kernel": 1.8199e9 + 0.5318e9,
+    "ft_segsum_light_kernel": 1.7194e9 + 0.3473e9,
 }
 DATA = ("synthetic: seeded random positions (kings + U{0..30} pieces), indices from the native restatement "
         "of the reference feature functions; W~N(0,0.01), bias=0, dOut~N(0,1)")

@@ -78,7 +78,7 @@ const char *nnue_ft_last_error(void);
 int nnue_ft_device_errors(uint32_t *flags, int clear);
 
 /* Tuning knobs (names: "fwd_chunk_vec", "fwd_items_per_warp", "fwd_unroll",
- * "fwd_min_blocks", "fwd_exact_chunks", "bwd_chunk_vec", "bwd_unroll",
+ * "fwd_min_blocks", "fwd_exact_chunks", "fwd_block", "bwd_chunk_vec", "bwd_unroll",
  * "bwd_min_blocks", "bwd_exact_chunks", "bwd_block", "bwd_variant",
  * "bwd_stream_cfg", "bwd_entries_per_warp", "heavy_threshold", "heavy_cap",
  * "sort_variant", "sort_blocks_per_sm", "sort_tile_rows", "sort_tile",

@@ -95,12 +95,12 @@ __device__ __forceinline__ int compact_rows(const int (&f)[kIdxGroups], int T, c
 // kernel is latency-bound: bytes in flight per SM are resident warps x D x
 // one row slice, so MINB (resident blocks the register budget is sized for)
 // matters as much as D.
-template <typename VT, int V, int D, int MINB = 1, bool MULTI = false>
-__global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParams p) {
+template <typename VT, int V, int D, int MINB = 1, bool MULTI = false, int BLOCK = kBlock>
+__global__ void __launch_bounds__(BLOCK, MINB) ft_forward_kernel(const FwdParams p) {
   using Ops = Vec<VT>;
   // one table: 32-bit row offsets; table set: row addresses
   using Entry = std::conditional_t<MULTI, const VT*, int>;
-  __shared__ Entry s_list[kWarpsPerBlock][32 * kIdxGroups];
+  __shared__ Entry s_list[BLOCK / 32][32 * kIdxGroups];
   const int lane = threadIdx.x & 31;
   Entry* list = s_list[threadIdx.x >> 5];
   const int chunk = p.chunk0 + blockIdx.y;
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(kBlock, MINB) ft_forward_kernel(const FwdParam
   const int row_vec = p.g.n_vec;
 
   const int64_t n_items = (int64_t)p.P * p.B;
-  int64_t item = ((int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5)) * p.items_per_warp;
+  int64_t item = ((int64_t)blockIdx.x * (BLOCK / 32) + (threadIdx.x >> 5)) * p.items_per_warp;
   const int64_t item_end = item + p.items_per_warp < n_items ? item + p.items_per_warp : n_items;
   if (item >= item_end) return;
   auto index_row = [&](int64_t it) {

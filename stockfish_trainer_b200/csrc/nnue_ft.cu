@@ -108,6 +108,7 @@ struct Tuning {
   int64_t sort_variant = 1;        // 1: counting placement + per-segment sort, 0: LSD radix passes
   int64_t sort_blocks_per_sm = 16;  // counting placement: grid of the two passes over the index arrays
   int64_t colsum_parts = 296;      // position ranges of the bias column sum
+  int64_t fwd_block = 128;         // forward (1 vector per lane, 4 blocks' registers): threads per block, 256 or 128
   int64_t bwd_block = 128;         // light rows: threads per block (256, 128 or 64; 1 vector per lane, 2-row batches)
 };
 Tuning g_tune;
@@ -140,6 +141,7 @@ ParamRef* params() {
       {"sort_tile", &g_tune.sort_tile, 32 * kSortBatch, 1 << 20},
       {"colsum_parts", &g_tune.colsum_parts, 1, 1 << 16},
       {"bwd_block", &g_tune.bwd_block, 64, 256},
+      {"fwd_block", &g_tune.fwd_block, 128, 256},
       {nullptr, nullptr, 0, 0},
   };
   return p;
@@ -178,6 +180,14 @@ void launch_forward_vd(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(warps, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
+  if constexpr (MINB == 4 && V == 1) {
+    if (g_tune.fwd_block == 128) {  // blocks of 4 warps, registers as for 4 blocks of 8
+      dim3 g4((unsigned)ceil_div(warps, 4), (unsigned)n_chunks);
+      if (p.tabs.n > 1) ft_forward_kernel<VT, V, D, 8, true, 128><<<g4, 128, 0, s>>>(p);
+      else ft_forward_kernel<VT, V, D, 8, false, 128><<<g4, 128, 0, s>>>(p);
+      return;
+    }
+  }
   if (p.tabs.n > 1) ft_forward_kernel<VT, V, D, MINB, true><<<grid, kBlock, 0, s>>>(p);
   else ft_forward_kernel<VT, V, D, MINB, false><<<grid, kBlock, 0, s>>>(p);
 }

@@ -94,6 +94,8 @@ def test_forward_empty_rows_and_batches(cuda):
         {"fwd_unroll": 8, "fwd_min_blocks": 2},
         {"fwd_unroll": 4, "fwd_min_blocks": 6},
         {"fwd_unroll": 6, "fwd_min_blocks": 5, "fwd_items_per_warp": 7},
+        {"fwd_block": 256},
+        {"fwd_block": 128, "fwd_items_per_warp": 5},
     ],
 )
 def test_forward_tuning_variants_bit_exact(cuda, params):

@@ -500,6 +500,14 @@ def run_ours(args):
         Wp = W.detach().clone().requires_grad_()
         bp = bias.detach().clone().requires_grad_()
 
+        def ft_pair(idx0, idx1):
+            # one GPU: the reference-facing autograd function; N GPUs: its
+            # data-parallel form, whose backward returns the averaged gradients
+            # with the exchange overlapped in row blocks
+            if world > 1:
+                return ddp.SparseLinearPairAllreduce.apply(idx0, idx1, Wp, bp, world, max(args.ddp_blocks, 1))
+            return SparseLinearPairFunction.apply(idx0, idx1, Wp, bp)
+
         # Inputs move on a copy stream one step ahead (double-buffered), as a
         # data loader feeding the GPU would: step k's copy overlaps step k-1's
         # compute, and step k waits only for its own copy.
@@ -521,14 +529,9 @@ def run_ours(args):
             cur = torch.cuda.current_stream(dev)
             cur.wait_event(copied[s])
             enqueue_copy(k + 1)
-            o0, o1 = SparseLinearPairFunction.apply(dbuf[s][0], dbuf[s][1], Wp, bp)
+            o0, o1 = ft_pair(dbuf[s][0], dbuf[s][1])
             consumed[s].record(cur)  # the indices are read by the forward and its index phase only
             torch.autograd.backward([o0, o1], [g0, g1])
-            if world > 1:
-                dist.all_reduce(Wp.grad)
-                dist.all_reduce(bp.grad)
-                Wp.grad.div_(world)
-                bp.grad.div_(world)
             host_out.copy_(bp.grad, non_blocking=True)
             Wp.grad = None
             bp.grad = None
@@ -551,13 +554,8 @@ def run_ours(args):
         def serial_step():
             d0 = h0.to(dev, non_blocking=True)
             d1 = h1.to(dev, non_blocking=True)
-            o0, o1 = SparseLinearPairFunction.apply(d0, d1, Wp, bp)
+            o0, o1 = ft_pair(d0, d1)
             torch.autograd.backward([o0, o1], [g0, g1])
-            if world > 1:
-                dist.all_reduce(Wp.grad)
-                dist.all_reduce(bp.grad)
-                Wp.grad.div_(world)
-                bp.grad.div_(world)
             host_out.copy_(bp.grad, non_blocking=True)
             Wp.grad = None
             bp.grad = None
@@ -600,13 +598,8 @@ def run_ours(args):
             enqueue_board_copy(k + 1)
             positions.encode_device(bbuf[s], args.feature_set, out=ibuf)
             bconsumed[s].record(cur)
-            o0, o1 = SparseLinearPairFunction.apply(ibuf[0], ibuf[1], Wp, bp)
+            o0, o1 = ft_pair(ibuf[0], ibuf[1])
             torch.autograd.backward([o0, o1], [g0, g1])
-            if world > 1:
-                dist.all_reduce(Wp.grad)
-                dist.all_reduce(bp.grad)
-                Wp.grad.div_(world)
-                bp.grad.div_(world)
             host_out.copy_(bp.grad, non_blocking=True)
             Wp.grad = None
             bp.grad = None
@@ -642,7 +635,8 @@ def run_ours(args):
         e2e = {"value": args.batch / (ms_e2e / 1e3), "unit": "positions/s",
                "h2d_bytes_per_step": int(h0.numel() * 4 + h1.numel() * 4), "d2h_bytes_per_step": C * 4,
                "ms_per_step": ms_e2e,
-               "path": "SparseLinearPairFunction autograd fwd+bwd; each step's indices copied from pinned "
+               "path": "SparseLinearPairFunction autograd fwd+bwd (N > 1: ddp.SparseLinearPairAllreduce, "
+                       "gradients averaged inside the backward); each step's indices copied from pinned "
                        "host memory on a copy stream one step ahead (double-buffered); bias grad read back",
                "serial_copy_ms_per_step": ms_serial,
                "boards": {"value": args.batch / (ms_boards / 1e3), "unit": "positions/s",

@@ -133,3 +133,47 @@ def backward_allreduce_overlapped(grad0, grad1, batch: int, max_active: int, buf
     if not avg:
         buf.flat.div_(world_size)
 
+
+
+class SparseLinearPairAllreduce(torch.autograd.Function):
+    """``SparseLinearPairFunction`` for data-parallel training.
+
+    (idx_white, idx_black, weight, bias, world_size, n_blocks, group) ->
+    (out_white, out_black).  The forward is the pair forward with the
+    backward's index phase beside it; the backward returns the dense weight
+    and bias gradients already averaged over the process group, with the
+    exchange overlapped with the gradient computation row block by row block
+    (``backward_allreduce_overlapped``).  This is the averaging the
+    reference's DDP applies to the FT parameters (src/train/common.py:186-199,
+    src/train/distributed.py:47-77), done inside the FT's own backward instead
+    of a second pass over the finished gradient, so those two parameters must
+    be left out of any other gradient averaging.  Every rank calls it with the
+    same shapes; world_size 1 gives the plain backward."""
+
+    @staticmethod
+    def forward(ctx, feature_indices_0, feature_indices_1, weight, bias, world_size: int = 1, n_blocks: int = 4,
+                group=None):
+        from .feature_transformer import functions
+
+        functions._check_inputs(feature_indices_0, weight, bias)
+        functions._check_inputs(feature_indices_1, weight, bias)
+        assert feature_indices_0.shape == feature_indices_1.shape
+        out0, out1, ws = functions._forward_pair(feature_indices_0, feature_indices_1, weight, bias)
+        ctx.workspace = ws
+        ctx.shapes = (tuple(feature_indices_0.shape), tuple(weight.shape))
+        ctx.world, ctx.blocks, ctx.group = int(world_size), int(n_blocks), group
+        return out0, out1
+
+    @staticmethod
+    def backward(ctx, grad0, grad1):
+        assert not ctx.needs_input_grad[0] and not ctx.needs_input_grad[1]
+        (B, K), (T, C) = ctx.shapes
+        ws, ctx.workspace = ctx.workspace, None
+        dev = ws.device
+        # a missing output gradient counts as zeros, so every rank runs the
+        # same collectives
+        g0 = grad0.contiguous() if grad0 is not None else torch.zeros(B, C, device=dev)
+        g1 = grad1.contiguous() if grad1 is not None else torch.zeros(B, C, device=dev)
+        buf = GradientBuffer(T, C, dev)
+        backward_allreduce_overlapped(g0, g1, B, K, buf, ws, ctx.world, n_blocks=ctx.blocks, group=ctx.group)
+        return None, None, buf.weight, buf.bias, None, None, None

@@ -92,3 +92,78 @@ def test_two_gpu_overlapped_allreduce_matches_shard_gradients(tmp_path, blocks):
     for r in range(world):
         np.testing.assert_array_equal(np.load(tmp_path / f"w{r}.npy"), expect_w)
         np.testing.assert_array_equal(np.load(tmp_path / f"b{r}.npy"), expect_b)
+
+
+def _autograd_worker(rank, world, port, out_dir):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from stockfish_trainer_b200 import ddp, positions
+
+    rt = ddp.init_from_env("nccl", timeout_s=60)
+    dev = torch.device("cuda", rt.local_rank)
+    T = positions.feature_set_info(FS)[1]
+    white, black, g0, g1, n = _inputs(rank, world)
+    W = torch.from_numpy(np.random.default_rng(3).standard_normal((T, C), dtype=np.float32) *
+                         np.float32(0.01)).to(dev).requires_grad_()
+    bias = torch.zeros(C, device=dev, requires_grad=True)
+    i0, i1 = torch.from_numpy(white).to(dev), torch.from_numpy(black).to(dev)
+    o0, o1 = ddp.SparseLinearPairAllreduce.apply(i0, i1, W, bias, world, 3)
+    torch.autograd.backward([o0, o1], [torch.from_numpy(g0).to(dev), torch.from_numpy(g1).to(dev)])
+    torch.cuda.synchronize()
+    np.save(os.path.join(out_dir, f"w{rank}.npy"), W.grad.cpu().numpy())
+    np.save(os.path.join(out_dir, f"b{rank}.npy"), bias.grad.cpu().numpy())
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_allreduce_autograd_function_matches_shard_gradients(tmp_path):
+    from stockfish_trainer_b200 import positions
+    from stockfish_trainer_b200.feature_transformer import ops
+
+    world = 2
+    mp.start_processes(_autograd_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    T = positions.feature_set_info(FS)[1]
+    dev = torch.device("cuda", 0)
+    shard = []
+    for r in range(world):
+        white, black, g0, g1, n = _inputs(r, world)
+        dW = torch.empty(T, C, device=dev)
+        dB = torch.empty(C, device=dev)
+        t = lambda a: torch.from_numpy(a).to(dev)
+        ops.backward_into(t(white), t(black), t(g0), t(g1), dW, dB, accumulate=False)
+        shard.append((dW.cpu().numpy(), dB.cpu().numpy()))
+    for r in range(world):
+        np.testing.assert_array_equal(np.load(tmp_path / f"w{r}.npy"), (shard[0][0] + shard[1][0]) / np.float32(2))
+        np.testing.assert_array_equal(np.load(tmp_path / f"b{r}.npy"), (shard[0][1] + shard[1][1]) / np.float32(2))
+
+
+def test_allreduce_autograd_function_single_rank_equals_pair_function(cuda):
+    """world_size 1: the same outputs and gradients as SparseLinearPairFunction,
+    bit for bit, also when one output gets no gradient."""
+    from stockfish_trainer_b200 import SparseLinearPairFunction, ddp, positions
+
+    T = positions.feature_set_info(FS)[1]
+    white, black, g0, g1, n = _inputs(0, 1)
+    i0, i1 = torch.from_numpy(white).to(cuda), torch.from_numpy(black).to(cuda)
+    W0 = torch.from_numpy(np.random.default_rng(3).standard_normal((T, C), dtype=np.float32) * np.float32(0.01))
+    b0 = torch.from_numpy(np.random.default_rng(4).standard_normal(C, dtype=np.float32))
+    for use_g1 in (True, False):
+        res = []
+        for fn in (lambda *a: SparseLinearPairFunction.apply(*a), lambda *a: ddp.SparseLinearPairAllreduce.apply(*a)):
+            W = W0.to(cuda).requires_grad_()
+            bias = b0.to(cuda).requires_grad_()
+            o0, o1 = fn(i0, i1, W, bias)
+            outs, grads = [o0], [torch.from_numpy(g0).to(cuda)]
+            if use_g1:
+                outs.append(o1)
+                grads.append(torch.from_numpy(g1).to(cuda))
+            torch.autograd.backward(outs, grads)
+            res.append((o0.detach().cpu(), o1.detach().cpu(), W.grad.cpu(), bias.grad.cpu()))
+        for a, b in zip(*res):
+            if a.shape == res[0][3].shape:
+                torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)  # bias grad: float64 column sums either way
+            else:
+                assert torch.equal(a, b)

@@ -4,23 +4,31 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
-Workload (the reference's headline configuration
-and [3]): Full_Threats+HalfKAv2_hm^ feature transformer, global batch 65536
-positions, L1 = 1040 + 8 PSQT columns (C = 1048), table 85296 x 1048 fp32,
-K = 160 padded int32 indices per perspective.  One step = forward of both
-perspectives + backward (dense weight gradient written once, bias gradient)
-and, for N > 1, the fp32 allreduce-mean of both gradients over NVLink.  The
-global batch is split evenly over ranks (strong scaling, like the reference's
-DDP path, src/train/common.py:256-263).
+Workload (the reference's headline configuration): Full_Threats+HalfKAv2_hm^
+feature transformer, global batch 65536 positions, L1 = 1040 + 8 PSQT
+columns (C = 1048), table 85296 x 1048 fp32, K = 160 padded int32 indices per
+perspective.  One step = forward of both perspectives + backward (dense
+weight gradient written once, bias gradient) and, for N > 1, the fp32
+allreduce-mean of both gradients over NVLink.  The global batch is split
+evenly over ranks (strong scaling, like the reference's DDP path,
+src/train/common.py:256-263).
 
 Inputs are synthetic: seeded random positions (stockfish_trainer_b200.positions)
 encoded by the native restatement of the reference's feature functions,
 W ~ N(0, 0.01), bias 0, dOut ~ N(0, 1).  All inputs (idx 84 MB, W 357 MB,
 dOut 550 MB) are larger than the 126 MB L2, so no flush between steps.
 
-Prints ONE JSON line on rank 0.  `--impl reference` times the CPU restatement
-of the reference path (oracle/, the reference has no CPU path of its own) on
-this host's cores instead.
+Prints ONE JSON line on rank 0.  Beside this library's numbers the line
+carries two baselines:
+* ``tilelang``: the reference's own SparseLinearFunction (TileLang kernels,
+  staged unmodified by oracle/build.py) timed on the same GPU and tensors in
+  a separate process that does not load this library (oracle/tilelang_timing.py),
+  with a bit-for-bit comparison of its outputs and weight gradient;
+* ``cpu_baseline``: the C restatement of the reference path (oracle/) on this
+  host's cores, the whole batch per step.
+``--impl reference`` prints the reference arm: that same CPU measurement as
+its own line, inputs built by the oracle's encoder (oracle/positions.py), so
+that process loads none of this library's code.
 """
 
 from __future__ import annotations
@@ -45,12 +53,11 @@ FEATURE_SET = "Full_Threats+HalfKAv2_hm^"
 L1, NPSQT = 1040, 8
 C = L1 + NPSQT
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
-# gather kernels in the default 1-GPU headline run, from a one-pass ncu
-# capture of that command (profiles/dram_traffic_headline_fullsize.md).
-TRAFFIC_HEADLINE: dict = {
-    "ft_forward_kernel": 1.8199e9 + 0.5318e9,
-    "ft_segsum_light_kernel": 1.7194e9 + 0.3473e9,
-}
+# gather kernels come from a one-pass ncu capture of the default 1-GPU
+# headline command, summarised in this file with a digest of the kernel
+# sources it was taken on; a capture whose digest differs from the current
+# sources is stale and is not reported.
+TRAFFIC_FILE = os.path.join("profiles", "dram_traffic_headline_fullsize.md")
 DATA = ("synthetic: seeded random positions (kings + U{0..30} pieces), indices from the native restatement "
         "of the reference feature functions; W~N(0,0.01), bias=0, dOut~N(0,1)")
 
@@ -64,10 +71,11 @@ def parse_args():
     p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe", "ranger22", "epilogue",
                                           "composed"],
                    default="headline",
-                   help="headline: BASELINE configs[2]/[3] (the driver's metric); halfka: configs[1] "
-                        "(HalfKAv2_hm^, B=16384, phases reported separately); quantized: configs[4] "
-                        "(int16 forward, HalfKAv2_hm^, B=65536); gather-probe: random-row gather bandwidth "
-                        "versus table size (the ceiling for the FT gathers)")
+                   help="headline: Full_Threats+HalfKAv2_hm^, B=65536 (the headline metric); halfka: HalfKAv2_hm^, "
+                        "B=16384 (phases reported separately); quantized: int16 forward, HalfKAv2_hm^, "
+                        "B=65536; gather-probe: random-row gather bandwidth versus table size (the ceiling "
+                        "for the FT gathers); ranger22, epilogue, composed: the FT optimizer step, the FT "
+                        "epilogue and the composed FT module")
     p.add_argument("--batch", type=int, default=65536, help="global batch (positions)")
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--feature-set", default=FEATURE_SET)
@@ -81,7 +89,40 @@ def parse_args():
     p.add_argument("--param", action="append", default=[], metavar="NAME=VALUE",
                    help="native tuning knob (see include/nnue_ft.h nnue_ft_set_param)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline time budget")
+    p.add_argument("--no-tilelang", action="store_true",
+                   help="skip the reference TileLang kernels timed on the same GPU (N = 1 only)")
+    p.add_argument("--tilelang-timeout", type=float, default=900.0)
     return p.parse_args()
+
+
+def kernel_sources_digest() -> str:
+    """sha256 (16 hex digits) over the CUDA sources of the native library."""
+    import hashlib
+
+    csrc = os.path.join(ROOT, "stockfish_trainer_b200", "csrc")
+    h = hashlib.sha256()
+    for name in sorted(os.listdir(csrc)):
+        if name.endswith((".cu", ".cuh", ".h", ".cpp")):
+            h.update(name.encode())
+            with open(os.path.join(csrc, name), "rb") as f:
+                h.update(f.read())
+    return h.hexdigest()[:16]
+
+
+def captured_traffic():
+    """The DRAM-traffic capture summarised in TRAFFIC_FILE: its JSON block
+    (per-launch bytes per kernel, the git head and kernel-source digest it was
+    taken on, the command), plus "current" = whether the digest matches the
+    sources of this checkout.  None if absent."""
+    try:
+        with open(os.path.join(ROOT, TRAFFIC_FILE)) as f:
+            text = f.read()
+        block = text.split("```json", 1)[1].split("```", 1)[0]
+        cap = json.loads(block)
+    except (OSError, IndexError, ValueError):
+        return None
+    cap["current"] = cap.get("sources_digest") == kernel_sources_digest()
+    return cap
 
 
 def hbm_peak():
@@ -160,36 +201,55 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_baseline(white, black, W_np, seed, budget_s, per_step=None):
-    import oracle
-
-    nt = host_threads()
-    T = W_np.shape[0]
-    n = min(len(white), per_step or 4096)
+def cpu_inputs(n: int, T: int, seed: int):
+    """Table and output gradients for the CPU legs (numpy, seeded)."""
     rng = np.random.default_rng(seed + 99)
+    W_np = (rng.standard_normal((T, C), dtype=np.float32) * np.float32(0.01)).astype(np.float32)
     g0 = rng.standard_normal((n, C), dtype=np.float32)
     g1 = rng.standard_normal((n, C), dtype=np.float32)
+    return W_np, g0, g1
+
+
+def cpu_step(white, black, W_np, g0, g1, nthreads: int) -> float:
+    """One step of the reference path restated on the CPU (oracle/ft_oracle.c,
+    OpenMP): the forward of both perspectives (kernel.py:93-103), then each
+    perspective's backward into its own zero-filled dense weight gradient in
+    the reference's order (functions.py:62-65, kernel.py:108-188, bias
+    :269), added once as autograd does.  Returns seconds."""
+    import oracle
+
     bias = np.zeros(C, np.float32)
-    w, b = np.ascontiguousarray(white[:n]), np.ascontiguousarray(black[:n])
+    t0 = time.perf_counter()
+    oracle.ft_forward(white, W_np, bias, nthreads=nthreads)
+    oracle.ft_forward(black, W_np, bias, nthreads=nthreads)
+    oracle.ft_backward_pair(white, black, g0, g1, W_np.shape[0], nthreads=nthreads)
+    return time.perf_counter() - t0
+
+
+CPU_SAMPLE = ("every step: the whole batch ({n} positions), forward of both perspectives + the reference's "
+              "backward (two zero-filled dense dW, one per perspective, added once) in the reference's "
+              "summation order; C restatement of the reference kernels (oracle/ft_oracle.c) with OpenMP")
+
+
+def cpu_baseline(white, black, T, seed, budget_s):
+    """The reference arm's measurement, run inside this arm on rank 0: whole
+    batch per step, median of up to 5 steps within ``budget_s`` (>= 2)."""
+    nt = host_threads()
+    n = white.shape[0]
+    W_np, g0, g1 = cpu_inputs(n, T, seed)
+    cpu_step(white, black, W_np, g0, g1, nt)  # first touch of the buffers
     times = []
     t_start = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        oracle.ft_forward(w, W_np, bias, nthreads=nt)
-        oracle.ft_forward(b, W_np, bias, nthreads=nt)
-        oracle.ft_backward_pair(w, b, g0, g1, T, nthreads=nt)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s or len(times) >= 10:
-            break
+    while len(times) < 2 or (time.perf_counter() - t_start < budget_s and len(times) < 5):
+        times.append(cpu_step(white, black, W_np, g0, g1, nt))
     t_med = statistics.median(times)
     return {
         "value": n / t_med,
         "unit": "positions/s",
         "cores": nt,
         "kind": "port",
-        "sample": f"{n} positions of the headline workload (both perspectives, fwd + bwd incl. the two dense "
-                  f"dW the reference allocates), median of {len(times)} reps, C oracle with OpenMP",
-        "ms_per_sample": t_med * 1e3,
+        "sample": CPU_SAMPLE.format(n=n) + f"; median of {len(times)} steps",
+        "ms_per_step": t_med * 1e3,
     }
 
 
@@ -213,42 +273,108 @@ def base_config(args, world, b_rank, T, K, nnz=None):
 
 
 # ---------------------------------------------------------------------------
+# the reference's TileLang kernels on the same GPU (separate process)
+# ---------------------------------------------------------------------------
+def row_checksums(x):
+    """Per-row checksum of fp32 bit patterns: sum_c bits(x[r, c]) * (c + 1),
+    int64 (the same function as oracle/tilelang_timing.py computes)."""
+    import torch
+
+    bits = x.contiguous().view(torch.int32).to(torch.int64)
+    w = torch.arange(1, x.shape[1] + 1, dtype=torch.int64, device=x.device)
+    return (bits * w).sum(dim=1).cpu().numpy()
+
+
+def tilelang_baseline(args, white, black, T, ours: dict, ours_ms: float):
+    """Runs oracle/tilelang_timing.py in a child process on the same GPU and
+    tensors (indices passed in a temporary file, W / g0 / g1 regenerated from
+    the same seeds) and compares its outputs and gradients with this arm's
+    through per-row bit checksums."""
+    import shutil
+    import tempfile
+
+    tmp = tempfile.mkdtemp(prefix="ft_tilelang_")
+    try:
+        idx_path = os.path.join(tmp, "indices.npz")
+        np.savez(idx_path, white=white, black=black)
+        out = os.path.join(tmp, "result.json")
+        cmd = [sys.executable, "-m", "oracle.tilelang_timing", "--indices", idx_path, "--seed", str(args.seed),
+               "--num-inputs", str(T), "--output-size", str(C), "--steps", str(max(args.steps, 20)),
+               "--warmup", str(max(args.warmup, 3)), "--out", out]
+        env = {k: v for k, v in os.environ.items()
+               if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT")}
+        try:
+            r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True,
+                               timeout=args.tilelang_timeout)
+        except subprocess.TimeoutExpired:
+            return {"unavailable": f"the TileLang run did not finish within {args.tilelang_timeout:.0f} s"}
+        if r.returncode != 0 or not os.path.exists(out):
+            tail = ((r.stderr or "") + (r.stdout or "")).strip().splitlines()[-3:]
+            return {"unavailable": f"the TileLang run exited {r.returncode}: {' | '.join(tail)}"}
+        with open(out) as f:
+            res = json.load(f)
+        sums = dict(np.load(out + ".npz"))
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    same_inputs = bool(np.array_equal(sums["W"], ours["W"]) and np.array_equal(sums["g"], ours["g"]))
+    bit_exact = {k: bool(np.array_equal(sums[k], ours[k])) for k in ("out0", "out1", "dW")}
+    db_diff = float(np.max(np.abs(sums["dB"].astype(np.float64) - ours["dB"].astype(np.float64))))
+    repo_so = [p for p in res["shared_objects"] if p.startswith(ROOT) or "torch_extensions" in p]
+    B = white.shape[0]
+    return {
+        "impl": "the reference's SparseLinearFunction (TileLang kernels of src/model/modules/feature_transformer/"
+                "kernel.py, staged unmodified), both perspectives on one table + autograd backward, as "
+                "composed.py:52-53 drives it",
+        "value": B / (res["ms_per_step"] / 1e3),
+        "unit": "positions/s",
+        "ms_per_step": res["ms_per_step"],
+        "ms_per_step_mean": res["ms_per_step_mean"],
+        "forward_ms": res["forward_ms"],
+        "ours_ms_per_step": ours_ms,
+        "speedup_ours_over_tilelang": res["ms_per_step"] / ours_ms,
+        "target_speedup": 2.0,
+        "same_inputs": same_inputs,
+        "bit_exact_vs_ours": bit_exact,
+        "bias_grad_max_abs_diff_vs_ours": db_diff,
+        "first_call_s": res["first_call_s"],
+        "steps": res["steps"],
+        "warmup": res["warmup"],
+        "timing": "CUDA events around each step on the current stream, median; the first call (TileLang "
+                  "autotune + JIT) excluded and reported as first_call_s",
+        "process": "child process (oracle/tilelang_timing.py) that does not import this library",
+        "shared_objects_from_this_repo": repo_so,
+        "gpu": res["gpu"],
+    }
+
+
+# ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
 def run_reference(args):
+    """The reference arm: the reference path restated on the CPU, on this
+    host's cores, over the whole workload of this arm's config every step.
+    The reference has no CPU implementation of its own (functions.py:21-25
+    asserts CUDA tensors), so the restatement in oracle/ is what runs.  Inputs
+    come from the oracle's own position generator and feature encoder
+    (oracle/positions.py), so this process loads none of this library's code.
+    Under torchrun only rank 0 works."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
-    from stockfish_trainer_b200 import positions
+    from oracle import features as oracle_features
+    from oracle import positions as oracle_positions
 
-    fid, T, K = positions.feature_set_info(args.feature_set)
-    n = 2048
-    white, black, _ = positions.synthetic_batch(n, args.feature_set, seed=args.seed)
-    rng = np.random.default_rng(args.seed)
-    W_np = (rng.standard_normal((T, C), dtype=np.float32) * np.float32(0.01)).astype(np.float32)
-    import oracle
-
-    g0 = rng.standard_normal((n, C), dtype=np.float32)
-    g1 = rng.standard_normal((n, C), dtype=np.float32)
-    bias = np.zeros(C, np.float32)
-
+    T, K = oracle_features.feature_set_sizes(args.feature_set)
     nt = host_threads()
-
-    def sample_step():
-        oracle.ft_forward(white, W_np, bias, nthreads=nt)
-        oracle.ft_forward(black, W_np, bias, nthreads=nt)
-        oracle.ft_backward_pair(white, black, g0, g1, T, nthreads=nt)
-
-    for _ in range(args.warmup):
-        sample_step()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        sample_step()
-        times.append(time.perf_counter() - t0)
+    white, black, _ = oracle_positions.synthetic_batch(args.batch, args.feature_set, seed=args.seed, processes=nt)
+    nnz = int((white >= 0).sum() + (black >= 0).sum())
+    W_np, g0, g1 = cpu_inputs(args.batch, T, args.seed)
+    for _ in range(max(args.warmup, 3)):
+        cpu_step(white, black, W_np, g0, g1, nt)
+    times = [cpu_step(white, black, W_np, g0, g1, nt) for _ in range(args.steps)]
     total = sum(times)
-    value = n * len(times) / total
+    value = args.batch * len(times) / total
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -256,17 +382,16 @@ def run_reference(args):
         "unit": "positions/s",
         "n_gpus": world,
         "steps": args.steps,
-        "warmup": args.warmup,
+        "warmup": max(args.warmup, 3),
         "ms_per_step": total / len(times) * 1e3,
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": DATA,
-        "config": base_config(args, world, args.batch // max(world, 1), T, K),
+        "config": base_config(args, world, args.batch // max(world, 1), T, K, nnz),
         "cpu_baseline": {"value": value, "unit": "positions/s", "cores": nt, "kind": "port",
-                         "sample": f"each step: {n} positions of the headline workload, fwd + bwd of both "
-                                   "perspectives (C restatement of the reference kernels, OpenMP)"},
+                         "sample": CPU_SAMPLE.format(n=args.batch)},
         "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -297,6 +422,11 @@ def run_ours(args):
     first, b_rank = ddp.shard(args.batch, rank, world)
     white, black, _ = positions.synthetic_batch(b_rank, args.feature_set, seed=args.seed, first=first)
     nnz_rank = int((white >= 0).sum() + (black >= 0).sum())
+    nnz_all = nnz_rank
+    if world > 1:
+        t_nnz = torch.tensor([nnz_rank], dtype=torch.int64, device=dev)
+        dist.all_reduce(t_nnz)
+        nnz_all = int(t_nnz.item())
 
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     W = torch.randn(T, C, device=dev, generator=gen) * 0.01
@@ -420,9 +550,11 @@ def run_ours(args):
     a_step_survey = (nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4) + \
                     (nnz_rank * C * 4 + 2 * b_rank * K * 4 + T * C * 4)
     # DRAM bytes per launch from a one-pass ncu capture of this exact command
-    # (profiles/dram_traffic_headline_fullsize.md); other shapes: not captured
-    traffic_ref = TRAFFIC_HEADLINE if (args.workload == "headline" and b_rank == 65536 and not args.param
-                                       and world == 1) else {}
+    # taken on the current kernel sources (other shapes: not captured)
+    capture = captured_traffic()
+    default_run = (args.workload == "headline" and b_rank == 65536 and not args.param and world == 1
+                   and args.feature_set == FEATURE_SET)
+    traffic_ref = capture["per_launch_bytes"] if (capture and capture["current"] and default_run) else {}
     kernels = {}
     for kind, name, a_bytes in ((_native.TIMED_FORWARD, "ft_forward_kernel", a_fwd),
                                 (_native.TIMED_LIGHT_ROWS, "ft_segsum_light_kernel", a_light),
@@ -434,9 +566,12 @@ def run_ours(args):
             continue
         launches_per_step = len(durations) / args.steps
         achieved_k = a_bytes / (per_step_ms / 1e3) / 1e9
+        traffic_k = traffic_ref.get(name)
         kernels[name] = {"ms_per_step": per_step_ms, "launches_per_step": launches_per_step,
                          "algorithmic_bytes": a_bytes, "achieved": achieved_k, "frac": achieved_k / peak,
-                         "traffic": traffic_ref.get(name)}
+                         "traffic": traffic_k,
+                         "dram_frac": (traffic_k / launches_per_step / (per_step_ms / launches_per_step / 1e3)
+                                       / 1e9 / peak) if traffic_k else None}
     # the forward alone, K launches with nothing beside it
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(max(args.steps, 1))]
@@ -488,7 +623,21 @@ def run_ours(args):
         roofline.update({"achieved": k["achieved"], "frac": k["frac"], "traffic": k["traffic"],
                          "kernel": f"{top} (largest device time per step, timed live in the step)",
                          "kernel_ms": k["ms_per_step"], "algorithmic_bytes": k["algorithmic_bytes"],
+                         "dram_frac": k["dram_frac"],
                          "frac_of_l2_gather_ceiling": k["frac_of_l2_gather_ceiling"]})
+    # frac counts every gathered row as HBM bytes (the byte model of the
+    # reference path); most gathers hit L2, so frac exceeds 1.  dram_frac is
+    # the measured DRAM traffic over the same duration, and the L2 gather
+    # ceiling is the bound these kernels actually meet.
+    roofline["frac_note"] = ("frac = algorithmic bytes (every gathered row counted as HBM traffic) / duration / "
+                             "HBM peak; it exceeds 1 because most row gathers hit L2. dram_frac = measured DRAM "
+                             "bytes / duration / HBM peak. frac_of_l2_gather_ceiling = achieved / the random-row "
+                             "gather bandwidth of a table the size of one column slice")
+    if capture:
+        roofline["traffic_source"] = {"file": TRAFFIC_FILE, "head": capture.get("head"),
+                                      "sources_digest": capture.get("sources_digest"),
+                                      "current_sources_digest": kernel_sources_digest(),
+                                      "used": bool(traffic_ref)}
     roofline["kernels"] = kernels
 
     # ---- e2e through the reference-facing autograd API, host buffers -------
@@ -652,7 +801,15 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(white, black, W.cpu().numpy(), args.seed, args.cpu_seconds)
+        cpu = cpu_baseline(white, black, T, args.seed, args.cpu_seconds)
+
+    tilelang = None
+    if rank == 0 and world == 1 and not args.no_tilelang:
+        # this arm's last timed step: outputs, dense dW and dB of the same tensors
+        ours_sums = {"out0": row_checksums(out0), "out1": row_checksums(out1), "dW": row_checksums(grads.weight),
+                     "dB": grads.bias.cpu().numpy(), "W": row_checksums(W),
+                     "g": np.concatenate([row_checksums(g0), row_checksums(g1)])}
+        tilelang = tilelang_baseline(args, white, black, T, ours_sums, ms_per_step)
 
     if rank == 0:
         metric = METRIC if args.workload == "headline" else \
@@ -670,10 +827,11 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "f32",
             "data": DATA,
-            "config": base_config(args, world, b_rank, T, K, int(nnz_rank)),
+            "config": base_config(args, world, b_rank, T, K, int(nnz_all)),
             "phases_ms": phase_ms,
             "roofline": roofline,
             "cpu_baseline": cpu,
+            "tilelang": tilelang,
             "e2e": e2e,
             "gpu_launches": int(launches),
             "gpu_launches_per_step": launches / max(args.steps, 1),
@@ -722,7 +880,7 @@ def run_gather_probe(args):
 
 
 def run_quantized(args):
-    """int16 quantised FT forward of both perspectives,
+    """int16 quantised FT forward of both perspectives (B = 65536),
     HalfKAv2_hm^ export tables (22528 x 1040 int16 + 8 int32 PSQT) produced
     from random fp32 weights by the serializer's quantisation."""
     import torch
@@ -774,7 +932,7 @@ def run_quantized(args):
 
 
 def run_ranger22(args):
-    """Ranger22 step of the FT parameters: the merged
+    """Ranger22 step of the FT parameters (src/ranger22/optimizer.py): the merged
     85296 x 1048 table and the 1048 bias, each one fused update per step,
     the lookahead blend fused into every 5th step as in training.  One step =
     Ranger22FT.step() over both parameters."""
@@ -840,7 +998,7 @@ def run_ranger22(args):
 
 
 def run_epilogue(args):
-    """FT epilogue (SURVEY 8(f) rank 3): NNUEModel._transform_inputs after the
+    """FT epilogue: NNUEModel._transform_inputs after the
     FT (model.py:93-115), forward + backward of both perspectives at the
     headline batch, one fused kernel each way."""
     import torch
@@ -915,7 +1073,7 @@ def run_epilogue(args):
 
 
 def run_composed(args):
-    """Module-level composed FT: ComposedFeatureTransformer
+    """Module-level composed FT (src/model/modules/features/composed.py): ComposedFeatureTransformer
     forward + backward through autograd at the headline size, the per-feature
     tables read in place (no merged copy), against the reference module's
     graph (torch.cat of the per-feature tables with the virtual rows repeated,
@@ -999,7 +1157,7 @@ def run_composed(args):
                    "l2": "inputs larger than L2, no flush"},
         "roofline": {"bound": "hbm", "achieved": a_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": a_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
-                     "kernel": "module step (SURVEY 8(d) A_step)", "algorithmic_bytes": a_bytes,
+                     "kernel": "module step (forward + backward byte model of the FT op)", "algorithmic_bytes": a_bytes,
                      "peak_source": f"{src} hbm_gbs"},
         "cat_path_same_gpu": {"ms_per_step": ms_cat, "value": B / (ms_cat / 1e3), "unit": "positions/s",
                               "what": "reference module graph (torch.cat + repeat) with this library's FT op"},

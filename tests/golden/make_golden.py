@@ -216,9 +216,11 @@ def ranger22_fixture(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py REFERENCE_CHECKOUT [ranger22|transform_inputs]")
     if len(sys.argv) > 2 and sys.argv[2] == "ranger22":
         ranger22_fixture(sys.argv[1])
     elif len(sys.argv) > 2 and sys.argv[2] == "transform_inputs":
         transform_inputs_fixture(sys.argv[1])
     else:
-        main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+        main(sys.argv[1])

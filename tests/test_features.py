@@ -128,3 +128,29 @@ def test_host_encoder_rejects_invalid_positions():
     assert np.all(w[2] == -1) and np.all(b[2] == -1)
     np.testing.assert_array_equal(w[[0, 3]], good_w[[0, 3]])
     np.testing.assert_array_equal(b[[0, 3]], good_b[[0, 3]])
+
+
+def test_oracle_position_generator_matches_native():
+    """oracle/positions.py restates the package's seeded generator: the same
+    boards and side to move for any (seed, first) slice, including positions
+    redrawn for exceeding 128 threat features."""
+    from oracle import positions as OP
+
+    for seed, first, n in ((2024, 0, 300), (7, 123_456, 200), (2**63 + 5, 10**9, 100)):
+        nb, ns = P.generate_positions(n, seed=seed, first=first)
+        ob, os_ = OP.generate_positions(n, seed=seed, first=first)
+        np.testing.assert_array_equal(ob, nb)
+        np.testing.assert_array_equal(os_, ns)
+
+
+def test_oracle_synthetic_batch_matches_native_in_worker_processes():
+    """The bench's CPU legs build their inputs with the oracle encoder in
+    spawned worker processes; the rows equal the native encoder's."""
+    from oracle import positions as OP
+
+    fs = "Full_Threats+HalfKAv2_hm^"
+    ow, ob, os_ = OP.synthetic_batch(256, fs, seed=99, first=4096, processes=2)
+    nw, nb, ns = P.synthetic_batch(256, fs, seed=99, first=4096)
+    np.testing.assert_array_equal(ow, nw)
+    np.testing.assert_array_equal(ob, nb)
+    np.testing.assert_array_equal(os_, ns)

@@ -104,11 +104,13 @@ def backward_allreduce_overlapped(grad0, grad1, batch: int, max_active: int, buf
     the last block's exchange is exposed.  The bias gradient travels with the
     last block (it sits after the weight in the flat buffer).  Requires
     ``backward_prepare`` (or ``forward_pair_prepare``) to have filled
-    ``workspace`` on the current stream."""
+    ``workspace`` on the current stream.  Without a process group (a single
+    process) it is the plain backward; with one, even of a single rank, the
+    row blocks and their collectives run."""
     from .feature_transformer import ops
 
     T, C = buf.weight.shape
-    if world_size <= 1:
+    if world_size <= 1 and group is None and not (dist.is_available() and dist.is_initialized()):
         ops.backward_apply(grad0, grad1, batch, max_active, buf.weight, buf.bias, False, workspace)
         return
     compute = torch.cuda.current_stream(buf.flat.device)

@@ -100,3 +100,20 @@ def test_encode_device_wrapper(cuda):
     np.testing.assert_array_equal(b.cpu().numpy(), hb)
     with pytest.raises(ValueError):
         P.encode_device(torch.from_numpy(board), "Full_Threats+HalfKAv2_hm^")
+
+
+@pytest.mark.parametrize("fs", FEATURE_SETS)
+def test_device_encoder_matches_python_oracle(cuda, fs):
+    """Device rows against the independent Python restatement of the
+    reference's feature functions (oracle/features.py), not only against the
+    host encoder that shares the device encoder's source: the reference FENs
+    and 400 seeded positions."""
+    board, _ = P.generate_positions(400, seed=4242)
+    boards = np.concatenate([np.array([F.parse_fen(f)[0] for f in FENS], np.uint8), board])
+    dw, db, dwc, dbc = _device_encode(torch.from_numpy(boards).to(cuda), boards.shape[0], fs, cuda)
+    assert _native.device_errors() == 0
+    for i in range(boards.shape[0]):
+        for color, rows, counts in ((F.WHITE, dw, dwc), (F.BLACK, db, dbc)):
+            row, count = F.encode(boards[i], color, fs)
+            np.testing.assert_array_equal(rows[i], np.array(row, np.int32))
+            assert counts[i] == count

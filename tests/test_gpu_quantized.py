@@ -70,3 +70,21 @@ def test_quantized_forward_wraps_like_int16(cuda):
     ra, rp = oracle.ft_quantized_forward(idx, wq, pq, bq, False)
     np.testing.assert_array_equal(acc.cpu().numpy(), ra)
     np.testing.assert_array_equal(ps.cpu().numpy(), rp)
+
+
+def test_quantized_forward_full_size(cuda):
+    """The int16 configuration at full size: HalfKAv2_hm^, B = 65536 positions,
+    both perspectives, export tables 22528 x (1040 int16 + 8 int32), every
+    accumulator and PSQT value."""
+    white, black, _ = feature_batch(65536, "HalfKAv2_hm^", seed=2024)
+    W, V = _tables(2025)
+    export = oracle.halfka_export_weights(W, V)
+    wq = oracle.quantize(export[:, :L1], 255.0, np.int16)
+    pq = oracle.quantize(export[:, L1:], 9600.0, np.int32)
+    bq = oracle.quantize(random_table(1, L1, seed=2026, std=0.05)[0], 255.0, np.int16)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    a0, a1, p0, p1 = ops.quantized_forward_pair(t(white), t(black), t(wq), t(pq), t(bq), True)
+    for idx, acc, ps in ((white, a0, p0), (black, a1, p1)):
+        ra, rp = oracle.ft_quantized_forward(idx, wq, pq, bq, True)
+        np.testing.assert_array_equal(acc.cpu().numpy(), ra)
+        np.testing.assert_array_equal(ps.cpu().numpy(), rp)

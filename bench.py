@@ -69,13 +69,14 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=["headline", "halfka", "quantized", "gather-probe", "ranger22", "epilogue",
-                                          "composed"],
+                                          "composed", "train"],
                    default="headline",
                    help="headline: Full_Threats+HalfKAv2_hm^, B=65536 (the headline metric); halfka: HalfKAv2_hm^, "
                         "B=16384 (phases reported separately); quantized: int16 forward, HalfKAv2_hm^, "
                         "B=65536; gather-probe: random-row gather bandwidth versus table size (the ceiling "
                         "for the FT gathers); ranger22, epilogue, composed: the FT optimizer step, the FT "
-                        "epilogue and the composed FT module")
+                        "epilogue and the composed FT module; train: forward + backward + optimizer step "
+                        "(row-sharded optimizer for N > 1)")
     p.add_argument("--batch", type=int, default=65536, help="global batch (positions)")
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--feature-set", default=FEATURE_SET)
@@ -698,6 +699,42 @@ def run_ours(args):
         barrier()
         ms_e2e = max_over_ranks(s2.elapsed_time(e2)) / args.steps
 
+        # An unchanged caller: the reference's module code with only its
+        # SparseLinearFunction import switched to this library's
+        # (composed.py:52-53 calls it once per perspective on one table; each
+        # call's backward writes its own dense weight gradient and autograd
+        # adds the two).  Same host copies; N = 1 only.
+        ms_unchanged = None
+        if world == 1:
+            from stockfish_trainer_b200 import SparseLinearFunction
+
+            def unchanged_step(k):
+                s = k % 2
+                cur = torch.cuda.current_stream(dev)
+                cur.wait_event(copied[s])
+                enqueue_copy(k + 1)
+                o0 = SparseLinearFunction.apply(dbuf[s][0], Wp, bp)
+                o1 = SparseLinearFunction.apply(dbuf[s][1], Wp, bp)
+                torch.autograd.backward([o0, o1], [g0, g1])
+                consumed[s].record(cur)  # the backward reads the indices again
+                host_out.copy_(bp.grad, non_blocking=True)
+                Wp.grad = None
+                bp.grad = None
+
+            k0 = n_warm + args.steps
+            for k in range(k0, k0 + n_warm):
+                unchanged_step(k)
+            barrier()
+            s6, e6 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s6.record()
+            for k in range(k0 + n_warm, k0 + n_warm + args.steps):
+                unchanged_step(k)
+            e6.record()
+            barrier()
+            ms_unchanged = s6.elapsed_time(e6) / args.steps
+            torch.cuda.current_stream(dev).wait_stream(copy_stream)  # the last prefetch
+            barrier()
+
         # the same step with each copy issued on the compute stream right before
         # its step (no overlap), for reference
         def serial_step():
@@ -788,6 +825,12 @@ def run_ours(args):
                        "gradients averaged inside the backward); each step's indices copied from pinned "
                        "host memory on a copy stream one step ahead (double-buffered); bias grad read back",
                "serial_copy_ms_per_step": ms_serial,
+               "unchanged_caller": None if ms_unchanged is None else {
+                   "value": args.batch / (ms_unchanged / 1e3), "unit": "positions/s", "ms_per_step": ms_unchanged,
+                   "h2d_bytes_per_step": int(h0.numel() * 4 + h1.numel() * 4), "d2h_bytes_per_step": C * 4,
+                   "path": "the reference's call pattern unchanged (composed.py:52-53): SparseLinearFunction once "
+                           "per perspective on one table, each backward writing its own dense weight gradient, "
+                           "autograd adding the two; same double-buffered host copies"},
                "boards": {"value": args.batch / (ms_boards / 1e3), "unit": "positions/s",
                           "ms_per_step": ms_boards, "h2d_bytes_per_step": int(hboard.numel()),
                           "d2h_bytes_per_step": C * 4,
@@ -1082,7 +1125,7 @@ def run_composed(args):
     from torch import nn
 
     from stockfish_trainer_b200 import _native, positions
-    from stockfish_trainer_b200.feature_transformer import SparseLinearPairFunction
+    from stockfish_trainer_b200.feature_transformer import SparseLinearFunction, SparseLinearPairFunction
     from stockfish_trainer_b200.feature_transformer.composed import ComposedFeatureTransformer
 
     dev = torch.device("cuda", 0)
@@ -1127,6 +1170,16 @@ def run_composed(args):
         for p in module.parameters():
             p.grad = None
 
+    def dropin_graph():
+        # the reference module's forward unchanged (composed.py:49-54), only
+        # SparseLinearFunction taken from this library
+        merged = torch.cat([f.merged_weight() for f in feats], dim=0)
+        o0 = SparseLinearFunction.apply(i0, merged, module.bias)
+        o1 = SparseLinearFunction.apply(i1, merged, module.bias)
+        torch.autograd.backward([o0, o1], [d0, d1])
+        for p in module.parameters():
+            p.grad = None
+
     def timeit(fn):
         for _ in range(max(args.warmup, 3)):
             fn()
@@ -1140,6 +1193,7 @@ def run_composed(args):
         return a.elapsed_time(e) / args.steps
 
     ms_cat = timeit(cat_path)
+    ms_dropin = timeit(dropin_graph)
     l0c = _native.launch_count()
     ms = timeit(fused)
     launches = _native.launch_count() - l0c
@@ -1159,10 +1213,128 @@ def run_composed(args):
                      "frac": a_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
                      "kernel": "module step (forward + backward byte model of the FT op)", "algorithmic_bytes": a_bytes,
                      "peak_source": f"{src} hbm_gbs"},
+        "unchanged_module_same_gpu": {"ms_per_step": ms_dropin, "value": B / (ms_dropin / 1e3),
+                                      "unit": "positions/s",
+                                      "what": "the reference module's forward unchanged (torch.cat + repeat, "
+                                              "SparseLinearFunction once per perspective, autograd adding the two "
+                                              "dense weight gradients) with this library's SparseLinearFunction"},
         "cat_path_same_gpu": {"ms_per_step": ms_cat, "value": B / (ms_cat / 1e3), "unit": "positions/s",
                               "what": "reference module graph (torch.cat + repeat) with this library's FT op"},
         "gpu_launches": int(launches),
     })
+    return 0
+
+
+def run_train(args):
+    """FT training step: forward of both perspectives (with the backward's
+    index phase beside it), backward, and the Ranger22 update (the reference
+    trainer's configuration) of the table and bias.  N = 1: dense gradients
+    then the fused update over the whole table.  N > 1: the row-sharded step
+    (reduce-scatter of each row block's averaged gradient, the update of this
+    rank's rows, all-gather of the updated rows), with the unsharded path
+    (allreduce of the whole gradient, then the update of the whole table on
+    every rank, as the reference's DDP does) timed beside it."""
+    import torch
+    import torch.distributed as dist
+
+    from stockfish_trainer_b200 import _native, ddp, optim, positions, sharded
+    from stockfish_trainer_b200.feature_transformer import ops
+
+    rt = ddp.init_from_env("nccl", timeout_s=180.0)
+    rank, world = rt.rank, rt.world_size
+    dev = torch.device("cuda", rt.local_rank)
+    torch.cuda.set_device(dev)
+    fid, T, K = positions.feature_set_info(args.feature_set)
+    first, b_rank = ddp.shard(args.batch, rank, world)
+    white, black, _ = positions.synthetic_batch(b_rank, args.feature_set, seed=args.seed, first=first)
+    nnz = torch.tensor([int((white >= 0).sum() + (black >= 0).sum())], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.all_reduce(nnz)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    W = torch.randn(T, C, device=dev, generator=gen) * 0.01
+    bias = torch.zeros(C, device=dev)
+    gen_r = torch.Generator(device=dev).manual_seed(args.seed + 1000 + rank)
+    g0 = torch.randn(b_rank, C, device=dev, generator=gen_r)
+    g1 = torch.randn(b_rank, C, device=dev, generator=gen_r)
+    i0, i1 = torch.from_numpy(white).to(dev), torch.from_numpy(black).to(dev)
+    o0, o1 = torch.empty(b_rank, C, device=dev), torch.empty(b_rank, C, device=dev)
+    ws = ops.alloc_workspace(b_rank, K, T, C, 2, dev)
+    lr = 8.75e-4
+    n_blocks = max(args.ddp_blocks, 1)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def measure(step):
+        """(ms per step, max over ranks; this library's launches in the timed steps)"""
+        for _ in range(max(args.warmup, 3)):
+            step()
+        barrier()
+        l0 = _native.launch_count()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        barrier()
+        return max_over_ranks(a.elapsed_time(b) / args.steps), _native.launch_count() - l0
+
+    # the unsharded step: whole gradient averaged, whole table updated on every rank
+    Wp, bp = torch.nn.Parameter(W.clone()), torch.nn.Parameter(bias.clone())
+    whole = optim.Ranger22FT([Wp, bp], lr=lr)
+    buf = ddp.GradientBuffer(T, C, dev)
+
+    def unsharded_step():
+        ops.forward_pair_prepare(i0, i1, Wp.data, bp.data, o0, o1, ws)
+        ddp.backward_allreduce_overlapped(g0, g1, b_rank, K, buf, ws, world, n_blocks=n_blocks) if world > 1 else \
+            ops.backward_apply(g0, g1, b_rank, K, buf.weight, buf.bias, False, ws)
+        Wp.grad, bp.grad = buf.weight, buf.bias
+        whole.step()
+
+    ms_whole, launches = measure(unsharded_step)
+    del whole, buf, Wp, bp
+    ms_sharded = None
+    if world > 1:
+        Ws, bs = W.clone(), bias.clone()
+        opt = sharded.ShardedRanger22FT(Ws, bs, lr, n_blocks=n_blocks)
+
+        def sharded_step():
+            ops.forward_pair_prepare(i0, i1, Ws, bs, o0, o1, ws)
+            opt.backward_step(g0, g1, b_rank, K, ws)
+
+        ms_sharded, launches = measure(sharded_step)
+    if _native.device_errors(clear=True):
+        raise RuntimeError("device error flags raised during the training-step bench")
+    ms = ms_sharded if ms_sharded is not None else ms_whole
+    if rank == 0:
+        emit({
+            "metric": f"positions/s FT training step (fwd+bwd+Ranger22 update of the FT table and bias) "
+                      f"{args.feature_set} @B={args.batch} L1={L1}",
+            "value": args.batch / (ms / 1e3), "unit": "positions/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": DATA,
+            "config": dict(base_config(args, world, b_rank, T, K, int(nnz.item())),
+                           workload="FT training step: forward + backward + Ranger22 update (trainer "
+                                    "configuration, lookahead every 5 steps)"
+                                    + (", optimizer state sharded by table rows (reduce-scatter / update / "
+                                       "all-gather per row block)" if world > 1 else "")),
+            "unsharded": {"ms_per_step": ms_whole, "value": args.batch / (ms_whole / 1e3), "unit": "positions/s",
+                          "what": "whole gradient allreduce-averaged (row blocks overlapped with the backward), "
+                                  "whole table updated on every rank"},
+            "gpu_launches": int(launches) if launches is not None else None,
+        })
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
@@ -1195,6 +1367,8 @@ def main():
         return run_epilogue(args)
     if args.workload == "composed":
         return run_composed(args)
+    if args.workload == "train":
+        return run_train(args)
     if args.workload == "quantized":
         return run_quantized(args)
     if args.workload == "gather-probe":

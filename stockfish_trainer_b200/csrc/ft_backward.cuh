@@ -633,6 +633,7 @@ struct SegParams {
   float* heavy_part;          // [heavy_cap, 2, n_vec] vectors: per-perspective sums of heavy rows
   unsigned* heavy_ticket;     // [heavy_cap, heavy_ticket_stride]: pair tickets (one per piece), zeroed per call
   int32_t heavy_ticket_stride;
+  int32_t persp_delta;        // queued light rows: dout[1] - dout[0] in vectors (the host checked the range)
 };
 
 // Decodes a sorted value of perspective q; out-of-range values (a corrupt
@@ -780,6 +781,205 @@ __global__ void __launch_bounds__(BLOCK, MINB) ft_segsum_light_kernel(const SegP
     for (int v = 0; v < V; ++v) Ops::add(tot[v], acc1[v]);
   }
   seg_write<VT, V>(p, f, c0 + lane, tot, ok, e1 > s0);
+}
+
+// Light rows, queued: one warp per (row, column chunk of <= 32 vectors), the
+// form used when each lane owns one 16-byte vector.  A row's entries of both
+// perspectives are contiguous in sorted_b ([s0, s1) perspective 0, [s1, e1)
+// perspective 1).  Up to kQueueList of them are loaded in one round trip and
+// turned into 32-bit row offsets from dout[0] (perspective 1 adds
+// persp_delta, the distance to dout[1] in vectors -- the host checked every
+// such offset fits in int32) in a per-warp shared-memory list; each lane
+// adds them to its own column pointer.  Each perspective's rows then stream through a D-slot register
+// queue, as in the forward: consuming slot d re-issues it with the entry D
+// further on, so D row slices stay in flight during the walk.  Perspective
+// 0's sum is parked in shared memory while perspective 1 is walked with the
+// same registers.  Each perspective is summed from zero in ascending b and
+// dW = acc0 + acc1 is written once: the same adds, in the same order, as
+// ft_segsum_light_kernel.
+constexpr int kQueueList = 256;
+
+// Offsets of entries [first, first + m) (m <= kQueueList) of the row starting
+// at s0 into list[0, m).  Entries at or past n0 belong to perspective 1.
+__device__ __forceinline__ void queue_offsets(const SegParams& p, int* list, int s0, int first, int m, int n0,
+                                              int lane) {
+  const int B = (int)p.B;  // the host guarantees B * row_vec < 2^31
+  const int row_vec = p.g.n_vec;
+  int v[kQueueList / 32];
+  const int32_t* __restrict__ sbp = p.sorted_b + (s0 + first) + lane;
+#pragma unroll
+  for (int g = 0; g < kQueueList / 32; ++g) v[g] = g * 32 + lane < m ? __ldg(sbp + g * 32) : 0;
+#pragma unroll
+  for (int g = 0; g < kQueueList / 32; ++g) {
+    const int j = g * 32 + lane;
+    if (j < m) {
+      const bool q = first + j >= n0;
+      int b = v[g] - (q ? B : 0);
+      if ((unsigned)b >= (unsigned)B) {  // corrupt workspace: flag, read row 0
+        flag_error(kErrBadSegment);
+        b = 0;
+      }
+      list[j] = b * row_vec + (q ? p.persp_delta : 0);
+    }
+  }
+  __syncwarp();
+}
+
+// acc + the rows at src + list[lo, hi), added one by one in list order.
+template <int D>
+__device__ __forceinline__ float4 queue_sum(const float4* __restrict__ src, const int* list, int lo, int hi,
+                                            bool ok, float4 acc) {
+  using Ops = Vec<float4>;
+  float4 w[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d)
+    if (lo + d < hi && ok) w[d] = Ops::ldg(src + list[lo + d]);
+  int j = lo;
+  for (; j + 2 * D <= hi; j += D) {  // every slot consumed and re-issued in range
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      if (ok) {
+        Ops::add(acc, w[d]);
+        w[d] = Ops::ldg(src + list[j + d + D]);
+      }
+  }
+  for (; j < hi; j += D) {
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      if (ok) {
+        if (j + d < hi) Ops::add(acc, w[d]);
+        if (j + d + D < hi) w[d] = Ops::ldg(src + list[j + d + D]);
+      }
+  }
+  return acc;
+}
+
+// Sum (from zero, in order) of entries [lo, hi) of a row longer than the
+// list -- only when rows past the heavy-row cap stay light, or with a raised
+// heavy-row threshold -- one entry at a time, straight from sorted_b (few
+// registers, so this path does not set the kernel's register budget).
+__device__ __forceinline__ float4 queue_sum_long(const int32_t* __restrict__ sorted_b, int B, int row_vec,
+                                              int persp_delta, const float4* __restrict__ src, int s0, int lo,
+                                              int hi, int n0, bool ok, int lane) {
+  using Ops = Vec<float4>;
+  float4 acc = Ops::zero();
+  for (int j0 = lo; j0 < hi; j0 += 32) {
+    const int cnt = hi - j0 < 32 ? hi - j0 : 32;
+    int o = 0;
+    if (lane < cnt) {
+      const bool q = j0 + lane >= n0;
+      int b = __ldg(sorted_b + s0 + j0 + lane) - (q ? B : 0);
+      if ((unsigned)b >= (unsigned)B) {
+        flag_error(kErrBadSegment);
+        b = 0;
+      }
+      o = b * row_vec + (q ? persp_delta : 0);
+    }
+    for (int u = 0; u < cnt; ++u) {
+      const int ou = __shfl_sync(kFull, o, u);
+      if (ok) Ops::add(acc, Ops::ldg(src + ou));
+    }
+  }
+  return acc;
+}
+
+// acc + the rows at src + (lane u's `g`) for u in [0, n), n <= 32: the same
+// queue fed from a register group of offsets by shuffles (short rows: no
+// shared-memory round trip before the first row load).
+template <int D>
+__device__ __forceinline__ float4 queue_sum_regs(const float4* __restrict__ src, int g, int n, bool ok,
+                                                 float4 acc) {
+  using Ops = Vec<float4>;
+  float4 w[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) {
+    const int o = __shfl_sync(kFull, g, d);
+    if (d < n && ok) w[d] = Ops::ldg(src + o);
+  }
+  int j = 0;
+  for (; j + 2 * D <= n; j += D) {
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      const int o = __shfl_sync(kFull, g, j + d + D);
+      if (ok) {
+        Ops::add(acc, w[d]);
+        w[d] = Ops::ldg(src + o);
+      }
+    }
+  }
+  for (; j < n; j += D) {
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      const int o = __shfl_sync(kFull, g, (j + d + D) & 31);
+      if (ok) {
+        if (j + d < n) Ops::add(acc, w[d]);
+        if (j + d + D < n) w[d] = Ops::ldg(src + o);
+      }
+    }
+  }
+  return acc;
+}
+
+template <int D, int MINB, int BLOCK>
+__global__ void __launch_bounds__(BLOCK, MINB) ft_segsum_lightq_kernel(const SegParams p) {
+  __shared__ int s_list[BLOCK / 32][kQueueList];
+  __shared__ float4 s_park[BLOCK / 32][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int* list = s_list[warp];
+  const int chunk = p.chunk0 + blockIdx.y;
+  const int c0 = p.g.begin(chunk);
+  const bool ok = lane < p.g.width(chunk);
+  int64_t f = p.row_begin + (int64_t)blockIdx.x * (BLOCK / 32) + warp;
+  if (f >= p.row_end) return;
+  const int P = p.P;
+  const int bnd = lane <= P ? p.seg_start[f * P + lane] : 0;
+  const int kind = p.row_kind[f];
+  const int s0 = __shfl_sync(kFull, bnd, 0);
+  const int s1 = __shfl_sync(kFull, bnd, 1);
+  const int e1 = __shfl_sync(kFull, bnd, P);
+  if (kind) return;
+  const int col = c0 + lane;
+  const float4* __restrict__ src = reinterpret_cast<const float4*>(p.dout[0]) + col;
+  const int n = e1 - s0, n0 = s1 - s0;
+  float4 acc;
+  if (n0 <= 32 && n - n0 <= 32) {
+    // short row: each perspective's offsets in one register, both loaded in one round trip
+    const int B = (int)p.B, row_vec = p.g.n_vec;
+    int b0 = lane < n0 ? __ldg(p.sorted_b + s0 + lane) : 0;
+    int b1 = lane < n - n0 ? __ldg(p.sorted_b + s1 + lane) - B : 0;
+    if ((unsigned)b0 >= (unsigned)B || (unsigned)b1 >= (unsigned)B) {  // corrupt workspace: flag, read row 0
+      flag_error(kErrBadSegment);
+      b0 = (unsigned)b0 < (unsigned)B ? b0 : 0;
+      b1 = (unsigned)b1 < (unsigned)B ? b1 : 0;
+    }
+    acc = queue_sum_regs<D>(src, b0 * row_vec, n0, ok, Vec<float4>::zero());
+    if (P == 2) {
+      s_park[warp][lane] = acc;
+      acc = queue_sum_regs<D>(src, b1 * row_vec + p.persp_delta, n - n0, ok, Vec<float4>::zero());
+      float4 t = s_park[warp][lane];
+      Vec<float4>::add(t, acc);
+      acc = t;
+    }
+  } else if (n <= kQueueList) {
+    queue_offsets(p, list, s0, 0, n, n0, lane);  // both perspectives in one round trip
+    acc = queue_sum<D>(src, list, 0, n0, ok, Vec<float4>::zero());
+    if (P == 2) {
+      s_park[warp][lane] = acc;
+      acc = queue_sum<D>(src, list, n0, n, ok, Vec<float4>::zero());
+      float4 t = s_park[warp][lane];
+      Vec<float4>::add(t, acc);
+      acc = t;
+    }
+  } else {
+    const int B = (int)p.B;
+    acc = queue_sum_long(p.sorted_b, B, p.g.n_vec, p.persp_delta, src, s0, 0, n0, n0, ok, lane);
+    if (P == 2)
+      Vec<float4>::add(acc, queue_sum_long(p.sorted_b, B, p.g.n_vec, p.persp_delta, src, s0, n0, n, n0, ok, lane));
+  }
+  float4 tot[1] = {acc};
+  const bool okv[1] = {ok};
+  f = p.row_begin + (int64_t)blockIdx.x * (BLOCK / 32) + warp;  // recomputed, not kept live through the walk
+  seg_write<float4, 1>(p, f, col, tot, okv, n > 0);
 }
 
 // Heavy rows: a long sum per column whose only order-preserving parallelism

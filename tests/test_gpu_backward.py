@@ -111,13 +111,29 @@ def _with_params(params, fn):
         {"sort_tile_rows": 1, "sort_tile": 512},
         {"sort_tile_rows": 7, "sort_tile": 1536},
         {"colsum_parts": 1},
-        {"bwd_unroll": 2, "bwd_min_blocks": 8},
-        {"bwd_unroll": 8, "bwd_min_blocks": 4},
-        {"bwd_unroll": 4, "bwd_min_blocks": 0},
+        {"bwd_queue": 0, "bwd_unroll": 2, "bwd_min_blocks": 8},
+        {"bwd_queue": 0, "bwd_unroll": 8, "bwd_min_blocks": 4},
+        {"bwd_queue": 0, "bwd_unroll": 4, "bwd_min_blocks": 0},
         {"bwd_unroll": 4, "bwd_min_blocks": 5, "bwd_chunk_vec": 64, "bwd_exact_chunks": 1},
-        {"bwd_block": 256},
-        {"bwd_block": 128},
-        {"bwd_block": 64},
+        {"bwd_queue": 0, "bwd_block": 256},
+        {"bwd_queue": 0, "bwd_block": 128},
+        {"bwd_queue": 0, "bwd_block": 64},
+        {"bwd_queue": 0, "heavy_threshold": 4, "heavy_cap": 3},
+        {"bwd_queue": 2, "bwd_queue_min_blocks": 16, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 3, "bwd_queue_min_blocks": 16, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 3, "bwd_queue_min_blocks": 12, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 4, "bwd_queue_min_blocks": 16, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 4, "bwd_queue_min_blocks": 12, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 4, "bwd_queue_min_blocks": 8, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 6, "bwd_queue_min_blocks": 12, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 6, "bwd_queue_min_blocks": 8, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 2, "bwd_block": 64, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 3, "bwd_block": 64, "bwd_queue_min_entries": 0},
+        # rows > 256 entries (the long-row path) and > 32 per perspective (the list path)
+        {"bwd_queue": 6, "bwd_queue_min_blocks": 8, "heavy_threshold": 4, "heavy_cap": 3, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 2, "heavy_threshold": 10**9, "bwd_queue_min_entries": 0},  # hot rows on the queued path
+        {"bwd_queue": 6, "bwd_queue_min_blocks": 8, "bwd_chunk_vec": 8, "bwd_queue_min_entries": 0},
+        {"bwd_queue": 2, "bwd_queue_min_entries": 10**9},  # the heuristic picks the batched kernel
     ],
 )
 def test_backward_tuning_and_heavy_rows(cuda, params):
@@ -252,3 +268,22 @@ def test_backward_long_segments(cuda, B, T):
     np.testing.assert_array_equal(dW, rW)
     np.testing.assert_allclose(dB, rB, rtol=RTOL, atol=ATOL)
 
+
+
+@pytest.mark.parametrize("queue", [0, 2, 6])
+def test_backward_gradients_in_reverse_memory_order(cuda, queue):
+    """The two perspectives' output gradients as views of one tensor, the
+    second below the first in memory: the queued light rows address both from
+    the first one's base with a negative distance."""
+    B, C, T = 2000, 1048, 24576
+    white, black, _ = feature_batch(B, "HalfKAv2_hm^", seed=61)
+    g = torch.randn(2, B, C, device=cuda, generator=torch.Generator(device=cuda).manual_seed(62))
+    g0, g1 = g[1], g[0]  # perspective 1's gradient sits before perspective 0's
+    dW = torch.empty(T, C, device=cuda)
+    dB = torch.empty(C, device=cuda)
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    _with_params({"bwd_queue": queue, "bwd_queue_min_blocks": 8, "bwd_queue_min_entries": 0},
+                 lambda: ops.backward_into(t(white), t(black), g0, g1, dW, dB, accumulate=False))
+    rW, rB = oracle.ft_backward_pair(white, black, g0.cpu().numpy(), g1.cpu().numpy(), T)
+    np.testing.assert_array_equal(dW.cpu().numpy(), rW)
+    np.testing.assert_allclose(dB.cpu().numpy(), rB, rtol=RTOL, atol=ATOL)

@@ -23,6 +23,19 @@
  *   - Floating point: fp32 only.  The forward and the weight gradient add in
  *     the reference's order (ascending k per position; ascending position per
  *     feature), so both are bit-identical to the reference kernels.
+ *   - Process-wide state (one per process, shared by every caller, thread and
+ *     stream):
+ *       * tuning (nnue_ft_set_param): a change applies to every later call in
+ *         the process; change it only while no call of this library is
+ *         running or being enqueued;
+ *       * one side stream per device, with one fork/join event pair: the
+ *         backward's heavy rows and bias sum run there beside the caller's
+ *         stream.  Calls from several streams stay correct but serialise
+ *         their side-stream work, and a join may wait for another stream's
+ *         side work too;
+ *       * the kernel timer and the sticky device error word.
+ *     The library keeps device-side objects (streams, events) per device for
+ *     the life of the process: do not call it across cudaDeviceReset.
  */
 #ifndef NNUE_FT_H
 #define NNUE_FT_H
@@ -169,12 +182,18 @@ int nnue_ft_forward_pair_prepare(const int32_t *idx0, const int32_t *idx1, int64
  *     host that reaches the GPU only through this C ABI with tensors owned by
  *     someone else and no way to provide a workspace.
  *   - Limit: sizes whose nnue_ft_backward_workspace_size() exceeds
- *     nnue_ft_noalloc_scratch_bytes() are rejected with NNUE_ERR_UNSUPPORTED
- *     (C = 1048: about 9K HalfKAv2_hm positions, about 1.2K
- *     Full_Threats+HalfKAv2_hm positions).
+ *     nnue_ft_noalloc_scratch_bytes() are rejected with NNUE_ERR_UNSUPPORTED.
+ *     With the default tuning that is about 9K HalfKAv2_hm positions, or
+ *     about 1.2K Full_Threats+HalfKAv2_hm positions, at C = 1048; tuning set
+ *     through nnue_ft_set_param (sort_tile, heavy_cap, colsum_parts,
+ *     sort_variant) changes the workspace size, so check
+ *     nnue_ft_backward_workspace_size() <= nnue_ft_noalloc_scratch_bytes()
+ *     for your shapes rather than rely on those counts, and do not change
+ *     tuning while a call may still be running.
  *   - The array exists on every GPU that loads the library until the process
- *     exits.  The first call on each device looks up its device address
- *     (and, like nnue_ft_backward, creates the library's side stream); make
+ *     exits.  Every call looks up its device address on the current device;
+ *     the first call on each device also loads the library's kernels there
+ *     and, like nnue_ft_backward, creates the library's side stream, so make
  *     that first call before any stream capture.
  *   - All calls share the one array and it keeps the previous call's
  *     contents (everything that must start at zero is cleared by each call).

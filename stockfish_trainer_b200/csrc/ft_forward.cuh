@@ -35,14 +35,15 @@ struct FwdParams {
   TableSet tabs;           // MULTI kernels: W split over separately allocated row blocks
 };
 
-constexpr int kIdxGroups = 8;  // index slots read per item in one go: 8 x 32 = 256
+constexpr int kIdxGroups = 8;  // index slots read per item in one go: 8 x 32 = 256 (at most)
 
-// Loads slots [32 * g0, 32 * (g0 + kIdxGroups)) of one index row, one group of
-// 32 per register, all loads in flight together.
+// Loads slots [32 * g0, 32 * (g0 + IG)) of one index row, one group of 32 per
+// register, all loads in flight together.
+template <int IG>
 __device__ __forceinline__ void load_index_groups(const int32_t* __restrict__ irow, int K, int g0, int lane,
-                                                  int (&f)[kIdxGroups]) {
+                                                  int (&f)[IG]) {
 #pragma unroll
-  for (int g = 0; g < kIdxGroups; ++g) {
+  for (int g = 0; g < IG; ++g) {
     const int k = (g0 + g) * 32 + lane;
     f[g] = k < K ? __ldcs(irow + k) : -1;
   }
@@ -50,11 +51,12 @@ __device__ __forceinline__ void load_index_groups(const int32_t* __restrict__ ir
 
 // Writes the valid indices of f[] (ascending slot order), times `scale`, to
 // `list`; returns how many.  Indices outside [-1, T) are flagged and dropped.
-__device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, int* list, int lane, int scale = 1) {
+template <int IG>
+__device__ __forceinline__ int compact_valid(const int (&f)[IG], int T, int* list, int lane, int scale = 1) {
   const unsigned lt = lanemask_lt();
   int n = 0;
 #pragma unroll
-  for (int g = 0; g < kIdxGroups; ++g) {
+  for (int g = 0; g < IG; ++g) {
     const bool valid = (unsigned)f[g] < (unsigned)T;
     if (!valid && f[g] != -1) flag_error(kErrBadIndex);
     const unsigned m = __ballot_sync(kFull, valid);
@@ -67,13 +69,13 @@ __device__ __forceinline__ int compact_valid(const int (&f)[kIdxGroups], int T, 
 
 // Table-set form of compact_valid: the list holds each valid row's address
 // in its own block (lane-independent: block base + local row + chunk start).
-template <typename VT>
-__device__ __forceinline__ int compact_rows(const int (&f)[kIdxGroups], int T, const TableSet& tabs, int row_vec,
+template <typename VT, int IG>
+__device__ __forceinline__ int compact_rows(const int (&f)[IG], int T, const TableSet& tabs, int row_vec,
                                             int c0, const VT** list, int lane) {
   const unsigned lt = lanemask_lt();
   int n = 0;
 #pragma unroll
-  for (int g = 0; g < kIdxGroups; ++g) {
+  for (int g = 0; g < IG; ++g) {
     const bool valid = (unsigned)f[g] < (unsigned)T;
     if (!valid && f[g] != -1) flag_error(kErrBadIndex);
     const unsigned m = __ballot_sync(kFull, valid);
@@ -95,12 +97,14 @@ __device__ __forceinline__ int compact_rows(const int (&f)[kIdxGroups], int T, c
 // kernel is latency-bound: bytes in flight per SM are resident warps x D x
 // one row slice, so MINB (resident blocks the register budget is sized for)
 // matters as much as D.
-template <typename VT, int V, int D, int MINB = 1, bool MULTI = false, int BLOCK = kBlock>
+// IG: index groups of 32 slots read per item in one go (IG * 32 >= K keeps
+// every item to one pass; fewer groups, fewer registers).
+template <typename VT, int V, int D, int MINB = 1, bool MULTI = false, int BLOCK = kBlock, int IG = kIdxGroups>
 __global__ void __launch_bounds__(BLOCK, MINB) ft_forward_kernel(const FwdParams p) {
   using Ops = Vec<VT>;
   // one table: 32-bit row offsets; table set: row addresses
   using Entry = std::conditional_t<MULTI, const VT*, int>;
-  __shared__ Entry s_list[BLOCK / 32][32 * kIdxGroups];
+  __shared__ Entry s_list[BLOCK / 32][32 * IG];
   const int lane = threadIdx.x & 31;
   Entry* list = s_list[threadIdx.x >> 5];
   const int chunk = p.chunk0 + blockIdx.y;
@@ -121,9 +125,9 @@ __global__ void __launch_bounds__(BLOCK, MINB) ft_forward_kernel(const FwdParams
     const int q = it >= p.B ? 1 : 0;
     return (q ? p.idx[1] : p.idx[0]) + (it - (int64_t)q * p.B) * p.K;
   };
-  const int n_super = (p.K + 32 * kIdxGroups - 1) / (32 * kIdxGroups);
-  int f[kIdxGroups];
-  load_index_groups(index_row(item), p.K, 0, lane, f);
+  const int n_super = (p.K + 32 * IG - 1) / (32 * IG);
+  int f[IG];
+  load_index_groups<IG>(index_row(item), p.K, 0, lane, f);
 
   for (; item < item_end; ++item) {
     const int persp = item >= p.B ? 1 : 0;
@@ -133,12 +137,12 @@ __global__ void __launch_bounds__(BLOCK, MINB) ft_forward_kernel(const FwdParams
 #pragma unroll
     for (int v = 0; v < V; ++v) acc[v] = ok[v] ? Ops::ldg(bvec + 32 * v) : Ops::zero();
     for (int sg = 0; sg < n_super; ++sg) {
-      if (sg > 0) load_index_groups(irow, p.K, sg * kIdxGroups, lane, f);
+      if (sg > 0) load_index_groups<IG>(irow, p.K, sg * IG, lane, f);
       int n;
-      if constexpr (MULTI) n = compact_rows<VT>(f, p.T, p.tabs, row_vec, c0, list, lane);
-      else n = compact_valid(f, p.T, list, lane, row_vec);
+      if constexpr (MULTI) n = compact_rows<VT, IG>(f, p.T, p.tabs, row_vec, c0, list, lane);
+      else n = compact_valid<IG>(f, p.T, list, lane, row_vec);
       // the next item's indices load while this item's rows are in flight
-      if (sg == n_super - 1 && item + 1 < item_end) load_index_groups(index_row(item + 1), p.K, 0, lane, f);
+      if (sg == n_super - 1 && item + 1 < item_end) load_index_groups<IG>(index_row(item + 1), p.K, 0, lane, f);
       VT w[D][V];
       auto row_ptr = [&](const Entry e) -> const VT* {
         if constexpr (MULTI) return e + lane;

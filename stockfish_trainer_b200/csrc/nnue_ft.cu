@@ -91,7 +91,7 @@ int check_launch(const char* what) {
 struct Tuning {
   int64_t fwd_chunk_vec = 32;       // forward column chunk, in 16-byte vectors
   int64_t fwd_items_per_warp = 16;  // (perspective, position) items per warp
-  int64_t fwd_unroll = 6;          // table rows in flight per warp (4, 6 or 8)
+  int64_t fwd_unroll = 6;          // table rows in flight per warp (4, 6 or 8; 5 groups: 2, 3, 4 or 6)
   int64_t bwd_unroll = 2;          // dOut rows per batch, light rows (2, 4 or 8)
   int64_t bwd_entries_per_warp = 2048;  // streaming backward: sorted entries per warp
   int64_t fwd_min_blocks = 4;      // forward: registers sized for 2..6 resident blocks (chunks <= 64 vectors)
@@ -115,6 +115,10 @@ struct Tuning {
   // queued light rows only when the expected entries per row, B * P * K / (4 T), reach this: on B200 the queue
   // is 7-8% faster at ~60 entries per row (B = 65536, Full_Threats+HalfKAv2_hm^), even at ~15 and 5% slower at ~8
   int64_t bwd_queue_min_entries = 32;
+  // forward, one vector per lane: index groups of 32 slots read per item, 1, 5 or 8; 0 = the fewest covering K
+  // (1 for K <= 32, 5 for K <= 160): on B200 5 groups instead of 8 made the K = 160 forward 4% faster
+  int64_t fwd_groups = 0;
+  int64_t fwd_queue_blocks = 8;    // forward with 1 or 5 groups: register budget for 8, 12 or 16 resident 128-thread blocks
 };
 Tuning g_tune;
 
@@ -128,7 +132,7 @@ ParamRef* params() {
   static ParamRef p[] = {
       {"fwd_chunk_vec", &g_tune.fwd_chunk_vec, 0, 1 << 20},
       {"fwd_items_per_warp", &g_tune.fwd_items_per_warp, 1, 1024},
-      {"fwd_unroll", &g_tune.fwd_unroll, 4, 8},
+      {"fwd_unroll", &g_tune.fwd_unroll, 2, 8},
       {"bwd_unroll", &g_tune.bwd_unroll, 2, 8},
       {"bwd_entries_per_warp", &g_tune.bwd_entries_per_warp, 32, 1 << 24},
       {"fwd_exact_chunks", &g_tune.fwd_exact_chunks, 0, 1},
@@ -150,6 +154,8 @@ ParamRef* params() {
       {"bwd_queue", &g_tune.bwd_queue, 0, 6},
       {"bwd_queue_min_blocks", &g_tune.bwd_queue_min_blocks, 8, 16},
       {"bwd_queue_min_entries", &g_tune.bwd_queue_min_entries, 0, int64_t(1) << 40},
+      {"fwd_groups", &g_tune.fwd_groups, 0, 8},
+      {"fwd_queue_blocks", &g_tune.fwd_queue_blocks, 8, 16},
       {nullptr, nullptr, 0, 0},
   };
   return p;
@@ -181,6 +187,29 @@ int lanes_per_row(const Geom& g) { return (g.max_width + 31) / 32; }
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
+// Forward, one vector per lane, IG index groups per item (K <= 32 * IG in
+// one pass): 128-thread blocks, register budget for BLOCKS resident blocks.
+template <typename VT, int IG, int D, int BLOCKS>
+void launch_forward_g(const FwdParams& p, dim3 g4, cudaStream_t s) {
+  if (p.tabs.n > 1) ft_forward_kernel<VT, 1, D, BLOCKS, true, 128, IG><<<g4, 128, 0, s>>>(p);
+  else ft_forward_kernel<VT, 1, D, BLOCKS, false, 128, IG><<<g4, 128, 0, s>>>(p);
+}
+
+template <typename VT, int IG>
+void launch_forward_g_any(const FwdParams& p, dim3 g4, cudaStream_t s) {
+  const int64_t b = g_tune.fwd_queue_blocks, d = g_tune.fwd_unroll;
+  if (b >= 16) {
+    if (d <= 2) launch_forward_g<VT, IG, 2, 16>(p, g4, s);
+    else launch_forward_g<VT, IG, 3, 16>(p, g4, s);
+  } else if (b >= 12) {
+    if (d <= 3) launch_forward_g<VT, IG, 3, 12>(p, g4, s);
+    else launch_forward_g<VT, IG, 4, 12>(p, g4, s);
+  } else {
+    if (d <= 4) launch_forward_g<VT, IG, 4, 8>(p, g4, s);
+    else launch_forward_g<VT, IG, 6, 8>(p, g4, s);
+  }
+}
+
 template <typename VT, int V, int D, int MINB>
 void launch_forward_vd(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
   const int64_t n_items = (int64_t)p.P * p.B;
@@ -188,6 +217,15 @@ void launch_forward_vd(FwdParams p, int chunk0, int n_chunks, cudaStream_t s) {
   p.chunk0 = chunk0;
   dim3 grid((unsigned)ceil_div(warps, kWarpsPerBlock), (unsigned)n_chunks);
   count_launch();
+  if constexpr (V == 1) {
+    const int64_t groups = g_tune.fwd_groups ? g_tune.fwd_groups : (p.K <= 32 ? 1 : p.K <= 160 ? 5 : 8);
+    if (groups < 8 && g_tune.fwd_block == 128) {
+      const dim3 g4((unsigned)ceil_div(warps, 4), (unsigned)n_chunks);
+      if (groups <= 1) launch_forward_g_any<VT, 1>(p, g4, s);
+      else launch_forward_g_any<VT, 5>(p, g4, s);
+      return;
+    }
+  }
   if constexpr (MINB == 4 && V == 1) {
     if (g_tune.fwd_block == 128) {  // blocks of 4 warps, registers as for 4 blocks of 8
       dim3 g4((unsigned)ceil_div(warps, 4), (unsigned)n_chunks);
@@ -886,30 +924,22 @@ void launch_qforward_v(const QFwdParams& p, cudaStream_t s) {
 // Scratch for nnue_ft_backward_noalloc: a fixed device array that exists on
 // every GPU that loads this library, for as long as the process lives.  Host
 // code must not pass the symbol itself to a kernel (on the host it is only a
-// stand-in); its device address comes from cudaGetSymbolAddress, looked up
-// once per device with that device current.
+// stand-in); its device address comes from cudaGetSymbolAddress with the
+// device current, looked up on every call (a cheap lookup, and never stale:
+// the first call on a device also loads the module there, which is why that
+// first call belongs before any stream capture).
 // ---------------------------------------------------------------------------
 static constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace nnue {
 namespace {
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
-
 int noalloc_scratch_address(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("backward_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(NNUE_ERR_UNSUPPORTED, "backward_noalloc: device ordinal %d >= 64", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(NNUE_ERR_CUDA, "backward_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    g_noalloc_addr[dev] = p;
-  }
-  *out = g_noalloc_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return fail(NNUE_ERR_CUDA, "backward_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  *out = p;
   return NNUE_OK;
 }
 }  // namespace

@@ -96,6 +96,16 @@ def test_forward_empty_rows_and_batches(cuda):
         {"fwd_unroll": 6, "fwd_min_blocks": 5, "fwd_items_per_warp": 7},
         {"fwd_block": 256},
         {"fwd_block": 128, "fwd_items_per_warp": 5},
+        {"fwd_groups": 8, "fwd_unroll": 4, "fwd_min_blocks": 6},
+        {"fwd_groups": 8},
+        {"fwd_groups": 5},
+        {"fwd_groups": 1},  # K = 160 read 32 slots at a time: several passes per item
+        {"fwd_groups": 5, "fwd_queue_blocks": 8, "fwd_unroll": 4},
+        {"fwd_groups": 5, "fwd_queue_blocks": 12, "fwd_unroll": 3},
+        {"fwd_groups": 5, "fwd_queue_blocks": 12, "fwd_unroll": 4},
+        {"fwd_groups": 5, "fwd_queue_blocks": 16, "fwd_unroll": 2},
+        {"fwd_groups": 1, "fwd_queue_blocks": 16, "fwd_unroll": 3, "fwd_items_per_warp": 3},
+        {"fwd_groups": 5, "fwd_chunk_vec": 8, "fwd_items_per_warp": 1},
     ],
 )
 def test_forward_tuning_variants_bit_exact(cuda, params):

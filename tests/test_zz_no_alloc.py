@@ -6,9 +6,10 @@ through the C ABI with tensors owned by another framework and nothing to hand
 over as a workspace.  For them the library keeps one fixed scratch array per
 GPU.  This test calls that entry point directly through the C ABI and checks
 it against the regular workspace entry point (nnue_ft_backward), twice in a
-row with different inputs so that contents left over from the first call
-cannot leak into the second.  It lives in its own file, named to be collected
-last, and passes both alone in a fresh process and after the other tests.
+row: the second call has another shape (feature set, batch and width), so the
+scratch layout moves and anything the first call left in the array lands in
+different fields.  It lives in its own file, named to be collected last, and
+passes both alone in a fresh process and after the other tests.
 """
 
 import ctypes
@@ -44,14 +45,17 @@ def _call_workspace(i0, i1, g0, g1, T, dW, dB, accumulate):
                                 dW.data_ptr(), dB.data_ptr(), int(accumulate), ws.data_ptr(), ws.numel(), stream)
 
 
-@pytest.mark.parametrize("fs,B", [("HalfKAv2_hm^", 2048), ("Full_Threats+HalfKAv2_hm^", 768)])
-def test_noalloc_backward_matches_workspace_backward_twice(cuda, fs, B):
-    C = 1048
-    T = positions.feature_set_info(fs)[1]
+@pytest.mark.parametrize("first,second", [
+    (("HalfKAv2_hm^", 2048, 1048), ("Full_Threats+HalfKAv2_hm^", 768, 264)),
+    (("Full_Threats+HalfKAv2_hm^", 768, 1048), ("HalfKAv2_hm^", 1500, 520)),
+])
+def test_noalloc_backward_matches_workspace_backward_twice(cuda, first, second):
     lib = _native.load()
-    assert lib.nnue_ft_backward_workspace_size(B, positions.feature_set_info(fs)[2], T, C, 2) <= \
-        lib.nnue_ft_noalloc_scratch_bytes()
-    for call, seed in enumerate((11, 12)):  # two calls in a row, different inputs
+    for call, (fs, B, C) in enumerate((first, second)):  # two calls in a row, different shapes
+        seed = 11 + call
+        T = positions.feature_set_info(fs)[1]
+        assert lib.nnue_ft_backward_workspace_size(B, positions.feature_set_info(fs)[2], T, C, 2) <= \
+            lib.nnue_ft_noalloc_scratch_bytes()
         white, black, _ = positions.synthetic_batch(B, fs, seed=seed)
         rng = np.random.default_rng(seed)
         g0 = torch.from_numpy(rng.standard_normal((B, C), dtype=np.float32)).to(cuda)

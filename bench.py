@@ -1197,6 +1197,17 @@ def run_composed(args):
     l0c = _native.launch_count()
     ms = timeit(fused)
     launches = _native.launch_count() - l0c
+    # the two module-level passes the composed step still runs around the FT
+    # kernels: the HalfKA table + virtual rows (one fp32 add per element) and
+    # the virtual rows' gradient (the sum over the 32 buckets of the HalfKA
+    # gradient, torch's repeat backward)
+    halfka = feats[1]
+    d_half = torch.randn(halfka.weight.shape, device=dev, generator=gen)
+    from stockfish_trainer_b200.feature_transformer import ops as ft_ops
+
+    ms_merge = timeit(lambda: ft_ops.merge_virtual(halfka.weight.detach(), halfka.virtual_weight.detach()))
+    reps = halfka.weight.shape[0] // halfka.virtual_weight.shape[0]
+    ms_vgrad = timeit(lambda: d_half.view(reps, -1, C).sum(0))
     nnz = int((white >= 0).sum() + (black >= 0).sum())
     T, K = 85296, white.shape[1]
     a_bytes = (nnz * C * 4 + 2 * B * C * 4 + 2 * B * K * 4) + (nnz * C * 4 + 2 * B * K * 4 + T * C * 4)
@@ -1213,6 +1224,10 @@ def run_composed(args):
                      "frac": a_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
                      "kernel": "module step (forward + backward byte model of the FT op)", "algorithmic_bytes": a_bytes,
                      "peak_source": f"{src} hbm_gbs"},
+        "module_passes_ms": {"halfka_virtual_merge": ms_merge, "virtual_grad_bucket_sum": ms_vgrad,
+                             "what": "the two passes around the FT kernels in the composed step: weight + "
+                                     "virtual rows (24576 x 1048, one add per element) and the virtual rows' "
+                                     "gradient (sum of the 32 bucket blocks of the HalfKA gradient)"},
         "unchanged_module_same_gpu": {"ms_per_step": ms_dropin, "value": B / (ms_dropin / 1e3),
                                       "unit": "positions/s",
                                       "what": "the reference module's forward unchanged (torch.cat + repeat, "

@@ -91,11 +91,12 @@ const char *nnue_ft_last_error(void);
 int nnue_ft_device_errors(uint32_t *flags, int clear);
 
 /* Tuning knobs (names: "fwd_chunk_vec", "fwd_items_per_warp", "fwd_unroll",
- * "fwd_min_blocks", "fwd_exact_chunks", "fwd_block", "bwd_chunk_vec", "bwd_unroll",
- * "bwd_min_blocks", "bwd_exact_chunks", "bwd_block", "bwd_variant",
- * "bwd_stream_cfg", "bwd_entries_per_warp", "heavy_threshold", "heavy_cap",
- * "sort_variant", "sort_blocks_per_sm", "sort_tile_rows", "sort_tile",
- * "colsum_parts"); unknown names and out-of-range values are rejected with
+ * "fwd_min_blocks", "fwd_exact_chunks", "fwd_block", "fwd_groups",
+ * "fwd_queue_blocks", "bwd_chunk_vec", "bwd_unroll", "bwd_min_blocks",
+ * "bwd_exact_chunks", "bwd_block", "bwd_queue", "bwd_queue_min_blocks",
+ * "bwd_queue_min_entries", "heavy_threshold", "heavy_cap",
+ * "sort_blocks_per_sm", "colsum_parts"); unknown names and out-of-range
+ * values are rejected with
  * NNUE_ERR_INVALID_ARGUMENT.  Every setting gives the same results.
  * Process-wide; change them only while no call is in flight and never between
  * a backward_prepare and its backward_apply. */
@@ -185,8 +186,8 @@ int nnue_ft_forward_pair_prepare(const int32_t *idx0, const int32_t *idx1, int64
  *     nnue_ft_noalloc_scratch_bytes() are rejected with NNUE_ERR_UNSUPPORTED.
  *     With the default tuning that is about 9K HalfKAv2_hm positions, or
  *     about 1.2K Full_Threats+HalfKAv2_hm positions, at C = 1048; tuning set
- *     through nnue_ft_set_param (sort_tile, heavy_cap, colsum_parts,
- *     sort_variant) changes the workspace size, so check
+ *     through nnue_ft_set_param (heavy_cap, colsum_parts) changes the
+ *     workspace size, so check
  *     nnue_ft_backward_workspace_size() <= nnue_ft_noalloc_scratch_bytes()
  *     for your shapes rather than rely on those counts, and do not change
  *     tuning while a call may still be running.

@@ -14,22 +14,16 @@
 // reference's two zero-initialised gradients added once.
 //
 // Pipeline (no host synchronisation anywhere, so it is graph-capturable):
-//   1. key = f * P + perspective.  A least-significant-digit radix sort of the
-//      (key, b) pairs, <= 10-bit digits.  Each digit pass is
-//        hist    : per warp tile, digit histogram  -> tile_hist[digit][tile]
-//        scan    : exclusive scan of tile_hist (digit-major) -> tile offsets
-//        scatter : each warp re-walks its tile in order; __match_any_sync
-//                  ranks equal digits within 32 lanes, a per-warp running
-//                  count in shared memory carries the rank across rounds.
-//      Tiles are walked in input order, so every pass is stable and the
-//      result is ordered by key with ties in original (ascending b) order.
-//      The first pass reads the raw [B, K] index arrays directly and also
-//      builds the full per-key histogram (-> segment offsets seg_start).
+//   1. index phase: key = f * P + perspective, value = perspective * B + b.
+//      A counting placement builds, for every key, the list of its positions
+//      in ascending b (the stable sort's order) plus the segment offsets
+//      seg_start (below: count, scan, place, order).
 //   2. classify: rows with more than `heavy_threshold` entries go to a heavy
-//      list (bounded); their work is split finer and scheduled first.
+//      list (bounded); their work is split finer and runs beside the rest.
 //   3. segsum: one warp per (row, column chunk); heavy rows one warp per
-//      (row, 32-vector piece).  Every row of dW is written exactly once
-//      (rows no position touches get 0), which replaces torch.zeros + RMW.
+//      (row, 32-vector piece, perspective).  Every row of dW is written
+//      exactly once (rows no position touches get 0), which replaces
+//      torch.zeros + read-modify-write.
 //   4. bias: deterministic column sum (per-part partials, fixed-order combine).
 #pragma once
 
@@ -38,22 +32,13 @@
 namespace nnue {
 
 // ----------------------------------------------------------------------------
-// Exclusive scan (int32), reduce-then-scan in three launches.  The length is
-// either host-known or derived on the device from a count (so passes after the
-// first can size themselves from the number of valid entries without a sync).
+// Exclusive scan (int32), reduce-then-scan in three launches.
 // ----------------------------------------------------------------------------
 struct ScanLen {
-  int64_t n;            // host length when `count` is null
-  const int32_t* count; // device entry count -> length = bins * ceil(count / tile)
-  int32_t tile;
-  int32_t bins;
+  int64_t n;  // elements
 };
 
-__device__ __forceinline__ int64_t scan_length(const ScanLen& L) {
-  if (!L.count) return L.n;
-  const int64_t tiles = ((int64_t)*L.count + L.tile - 1) / L.tile;
-  return tiles * L.bins;
-}
+__device__ __forceinline__ int64_t scan_length(const ScanLen& L) { return L.n; }
 
 constexpr int kScanItems = 16;
 constexpr int kScanTile = kBlock * kScanItems;
@@ -124,7 +109,7 @@ __global__ void __launch_bounds__(kBlock) scan_down_kernel(const int32_t* in, in
 }
 
 // ----------------------------------------------------------------------------
-// Radix passes
+// The raw [B, K] index arrays of both perspectives
 // ----------------------------------------------------------------------------
 struct RawSrc {
   const int32_t* idx[2];  // [B, K] per perspective
@@ -134,214 +119,9 @@ struct RawSrc {
   int32_t P;
 };
 
-struct PassParams {
-  RawSrc raw;                // first pass: read the raw index arrays
-  const int32_t* in_keys;    // later passes
-  const int32_t* in_vals;
-  const int32_t* count;      // later passes: device count of valid entries
-  int32_t tile;              // first pass: index rows per warp; later: entries per warp (multiple of 32*kSortBatch)
-  int32_t shift;             // digit = (key >> shift) & (bins - 1)
-  int32_t bits;
-  int32_t* tile_hist;        // [bins][n_tiles]
-  int32_t* key_count;        // first pass: full histogram over keys (may be null)
-  int32_t* out_keys;         // null on the last pass
-  int32_t* out_vals;
-  int64_t out_cap;           // capacity of out_keys / out_vals
-};
-
-constexpr int kSortBatch = 16;  // 32-slot chunks loaded before they are processed
-
-// ---- first pass: walk the raw [P][B][K] index arrays row by row ------------
-// A warp tile is `tile` consecutive index rows (perspective-major, then
-// position).  Each row is read in chunks of 32 slots, kSortBatch chunks per
-// batch of loads; a chunk with no valid slot (the -1 tail) costs one ballot.
-// Entries are visited in (perspective, position, slot) order, so ranks are
-// stable.
-struct RowWalk {
-  int64_t row;  // global row = perspective * B + position
-  int kc;       // 32-slot chunk inside the row
-};
-
-__device__ __forceinline__ void raw_load_batch(const PassParams& p, RowWalk w, int64_t r_end, int KC, int lane,
-                                               int (&f)[kSortBatch], int (&persp)[kSortBatch],
-                                               int (&b)[kSortBatch]) {
-  const int64_t B = p.raw.n_raw / (p.raw.K > 0 ? p.raw.K : 1);
-#pragma unroll
-  for (int r = 0; r < kSortBatch; ++r) {
-    f[r] = -1;
-    persp[r] = 0;
-    b[r] = 0;
-    if (w.row < r_end) {
-      const int q = w.row >= B ? 1 : 0;
-      const int64_t pos = w.row - q * B;
-      const int k = w.kc * 32 + lane;
-      persp[r] = q;
-      b[r] = (int)pos;
-      if (k < p.raw.K) f[r] = __ldcs((q ? p.raw.idx[1] : p.raw.idx[0]) + pos * p.raw.K + k);
-      if (++w.kc == KC) {
-        w.kc = 0;
-        ++w.row;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ RowWalk advance(RowWalk w, int KC, int n) {
-  const int64_t t = (int64_t)w.kc + n;
-  w.row += t / KC;
-  w.kc = (int)(t % KC);
-  return w;
-}
-
-__global__ void __launch_bounds__(kBlock) sort_hist_rows_kernel(const PassParams p) {
-  extern __shared__ int32_t sh[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bins = 1 << p.bits;
-  int32_t* h = sh + warp * bins;
-  for (int i = lane; i < bins; i += 32) h[i] = 0;
-  __syncwarp();
-  const int64_t rows = (int64_t)p.raw.P * (p.raw.n_raw / (p.raw.K > 0 ? p.raw.K : 1));
-  const int64_t n_tiles = (rows + p.tile - 1) / p.tile;
-  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (tile >= n_tiles) return;
-  const int KC = (p.raw.K + 31) / 32;
-  const int64_t r0 = tile * p.tile;
-  const int64_t r1 = r0 + p.tile < rows ? r0 + p.tile : rows;
-  for (RowWalk w{r0, 0}; w.row < r1; w = advance(w, KC, kSortBatch)) {
-    int f[kSortBatch], persp[kSortBatch], b[kSortBatch];
-    raw_load_batch(p, w, r1, KC, lane, f, persp, b);
-#pragma unroll
-    for (int r = 0; r < kSortBatch; ++r) {
-      const bool valid = (unsigned)f[r] < (unsigned)p.raw.T;
-      if (!valid && f[r] != -1) flag_error(kErrBadIndex);
-      if (__ballot_sync(kFull, valid) == 0) continue;
-      if (valid) {
-        const int key = f[r] * p.raw.P + persp[r];
-        atomicAdd(&h[(key >> p.shift) & (bins - 1)], 1);
-        if (p.key_count) atomicAdd(&p.key_count[key], 1);
-      }
-    }
-  }
-  __syncwarp();
-  for (int i = lane; i < bins; i += 32) p.tile_hist[(int64_t)i * n_tiles + tile] = h[i];
-}
-
-// Appends one 32-wide round of (key, value) pairs to the per-digit runs.
-__device__ __forceinline__ void scatter_round(const PassParams& p, int32_t* h, int bins, bool valid, int key, int val,
-                                              unsigned lt) {
-  const int digit = valid ? ((key >> p.shift) & (bins - 1)) : bins;  // `bins` = no digit
-  const unsigned peers = __match_any_sync(kFull, digit);
-  const int rank = __popc(peers & lt);
-  const int dst0 = valid ? h[digit] : 0;
-  __syncwarp();
-  if (valid) {
-    const int dst = dst0 + rank;
-    if ((unsigned long long)(unsigned)dst < (unsigned long long)p.out_cap) {
-      if (p.out_keys) p.out_keys[dst] = key;
-      p.out_vals[dst] = val;
-    } else {
-      flag_error(kErrBadSegment);
-    }
-    if (rank == 0) h[digit] = dst0 + __popc(peers);
-  }
-  __syncwarp();
-}
-
-__global__ void __launch_bounds__(kBlock) sort_scatter_rows_kernel(const PassParams p) {
-  extern __shared__ int32_t sh[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bins = 1 << p.bits;
-  int32_t* h = sh + warp * bins;  // running destination per digit
-  const int64_t rows = (int64_t)p.raw.P * (p.raw.n_raw / (p.raw.K > 0 ? p.raw.K : 1));
-  const int64_t n_tiles = (rows + p.tile - 1) / p.tile;
-  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (tile >= n_tiles) return;
-  // tile_hist now holds the scanned offsets: start of (digit, tile).
-  for (int i = lane; i < bins; i += 32) h[i] = p.tile_hist[(int64_t)i * n_tiles + tile];
-  __syncwarp();
-  const int KC = (p.raw.K + 31) / 32;
-  const int64_t r0 = tile * p.tile;
-  const int64_t r1 = r0 + p.tile < rows ? r0 + p.tile : rows;
-  const unsigned lt = lanemask_lt();
-  for (RowWalk w{r0, 0}; w.row < r1; w = advance(w, KC, kSortBatch)) {
-    int f[kSortBatch], persp[kSortBatch], b[kSortBatch];
-    raw_load_batch(p, w, r1, KC, lane, f, persp, b);
-#pragma unroll
-    for (int r = 0; r < kSortBatch; ++r) {
-      const bool valid = (unsigned)f[r] < (unsigned)p.raw.T;
-      if (__ballot_sync(kFull, valid) == 0) continue;
-      const int64_t B = p.raw.n_raw / p.raw.K;
-      scatter_round(p, h, bins, valid, f[r] * p.raw.P + persp[r], (int)(persp[r] * B + b[r]), lt);
-    }
-  }
-}
-
-// ---- later passes: flat (key, value) arrays of device-known length ---------
-__global__ void __launch_bounds__(kBlock) sort_hist_kernel(const PassParams p) {
-  extern __shared__ int32_t sh[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bins = 1 << p.bits;
-  int32_t* h = sh + warp * bins;
-  for (int i = lane; i < bins; i += 32) h[i] = 0;
-  __syncwarp();
-  const int64_t n_src = *p.count;
-  const int64_t n_tiles = (n_src + p.tile - 1) / p.tile;
-  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (tile >= n_tiles) return;  // whole warp
-  const int64_t e0 = tile * p.tile;
-  const int64_t e1 = e0 + p.tile < n_src ? e0 + p.tile : n_src;
-  for (int64_t base = e0; base < e1; base += 32 * kSortBatch) {
-    int key[kSortBatch];
-#pragma unroll
-    for (int r = 0; r < kSortBatch; ++r) {
-      const int64_t e = base + r * 32 + lane;
-      key[r] = e < e1 ? __ldg(p.in_keys + e) : -1;
-    }
-#pragma unroll
-    for (int r = 0; r < kSortBatch; ++r)
-      if (key[r] >= 0) atomicAdd(&h[(key[r] >> p.shift) & (bins - 1)], 1);
-  }
-  __syncwarp();
-  for (int i = lane; i < bins; i += 32) p.tile_hist[(int64_t)i * n_tiles + tile] = h[i];
-}
-
-__global__ void __launch_bounds__(kBlock) sort_scatter_kernel(const PassParams p) {
-  extern __shared__ int32_t sh[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bins = 1 << p.bits;
-  int32_t* h = sh + warp * bins;  // running destination per digit
-  const int64_t n_src = *p.count;
-  const int64_t n_tiles = (n_src + p.tile - 1) / p.tile;
-  const int64_t tile = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
-  if (tile >= n_tiles) return;
-  for (int i = lane; i < bins; i += 32) h[i] = p.tile_hist[(int64_t)i * n_tiles + tile];
-  __syncwarp();
-  const int64_t e0 = tile * p.tile;
-  const int64_t e1 = e0 + p.tile < n_src ? e0 + p.tile : n_src;
-  const unsigned lt = lanemask_lt();
-  for (int64_t base = e0; base < e1; base += 32 * kSortBatch) {
-    int key[kSortBatch], val[kSortBatch];
-#pragma unroll
-    for (int r = 0; r < kSortBatch; ++r) {
-      const int64_t e = base + r * 32 + lane;
-      key[r] = -1;
-      val[r] = 0;
-      if (e < e1) {
-        key[r] = __ldg(p.in_keys + e);
-        val[r] = __ldg(p.in_vals + e);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < kSortBatch; ++r) {
-      if (base + r * 32 >= e1) break;  // uniform
-      scatter_round(p, h, bins, key[r] >= 0, key[r], val[r], lt);
-    }
-  }
-}
-
 // ----------------------------------------------------------------------------
-// Counting placement (sort_variant 1): the same (key -> ascending b) lists as
-// the radix passes, built as a sparse transpose.
+// Counting placement: per key, the list of its positions in ascending b (the
+// order of the reference's stable sort), built as a sparse transpose.
 //   count : one pass over the raw index arrays, seg[key] += 1 per valid slot
 //   scan  : exclusive scan -> seg_start; cursor = copy of seg_start
 //   place : second pass; slot = atomicAdd(cursor[key], 1), values land in
@@ -349,7 +129,7 @@ __global__ void __launch_bounds__(kBlock) sort_scatter_kernel(const PassParams p
 //   order : every segment is sorted ascending (values of one key share the
 //           perspective, so ascending value = ascending b).  Equal values are
 //           the same position twice, so the order among them cannot change
-//           any sum; the result equals the stable radix sort.
+//           any sum; the result equals the stable sort.
 //           n <= 256: one warp, bitonic network in registers;
 //           n <= kSegSmem: one block, bitonic network in shared memory;
 //           larger: one block counts positions in shared-memory windows.
@@ -591,21 +371,6 @@ __global__ void classify_rows_kernel(const int32_t* __restrict__ seg_start, int3
   row_kind[f] = kind;
 }
 
-// Streaming work split: warp w owns the rows whose first entry lies in
-// [w * epw, (w + 1) * epw), i.e. rows [first_row[w], first_row[w + 1]).
-// Row f is the first row of every w with seg(f - 1) < w * epw <= seg(f), so
-// each first_row entry has exactly one writer.  n_warps is the grid's
-// capacity; warps past the last entry get empty ranges (first_row = T).
-__global__ void warp_ranges_kernel(const int32_t* __restrict__ seg_start, int32_t T, int32_t P, int32_t epw,
-                                   int32_t n_warps, int32_t* __restrict__ first_row) {
-  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (f > T) return;
-  const int64_t prev = f == 0 ? -1 : seg_start[(f - 1) * P];
-  const int64_t lo = f == 0 ? 0 : prev / epw + 1;
-  const int64_t hi = f == T ? n_warps : seg_start[f * P] / epw;
-  for (int64_t w = lo; w <= hi && w <= n_warps; ++w) first_row[w] = (int32_t)f;
-}
-
 // ----------------------------------------------------------------------------
 // Segment sums.  Sorted values encode (perspective, position) as
 // perspective * B + b, so a load can be issued from the value alone.
@@ -617,7 +382,6 @@ struct SegParams {
   const int32_t* heavy_list;  // walk path only
   const int32_t* n_heavy;
   const uint8_t* row_kind;
-  const int32_t* first_row;   // stream path: [n_stream_warps + 1]
   float* dW;                  // [T, C]
   int64_t B;                  // positions per perspective
   int32_t T;
@@ -625,7 +389,6 @@ struct SegParams {
   int32_t accumulate;         // 0: dW[f] = sum (all rows written); 1: dW[f] += sum (touched rows)
   int32_t heavy_cap;
   int32_t chunk0;             // first column chunk of this launch (blockIdx.y offset)
-  int32_t n_stream_warps;
   int32_t row_begin;          // rows [row_begin, row_end) of dW are produced by this call
   int32_t row_end;
   Geom g;
@@ -1069,148 +832,6 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
   }
   const VT t1[1] = {tot};
   seg_write<VT, 1>(p, f, col, t1, ok, true);
-}
-
-// ---------------------------------------------------------------------------
-// Streaming segment sums (fast path: 16-byte vectors, chunks of <= 32 x SV
-// vectors).  Each warp owns a contiguous range of rows holding about
-// `entries per warp` entries; because rows are in key order, their entries
-// are one contiguous run of the sorted list.  The warp streams that run
-// through a lane-private cp.async ring kStreamStages entries deep (SV
-// vectors per lane per entry), adding each arriving dOut slice to the
-// current (row, perspective) accumulator and finishing a row when its last
-// segment ends -- the pipeline never drains between rows, and hot rows need
-// no special path.  Values decode to (perspective, position) at issue time;
-// the consume side walks the segment table, 32 boundaries per load.
-// ---------------------------------------------------------------------------
-// 16-byte cp.async, skipped entirely when !pred (the destination keeps its
-// old bytes; callers never use them).
-__device__ __forceinline__ void cp_async16_if(float4* smem_dst, const float4* gsrc, bool pred) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p cp.async.cg.shared.global [%0], [%1], 16;\n}\n" ::"r"(d),
-      "l"(gsrc), "r"((int)pred)
-      : "memory");
-}
-
-// S: ring stages per warp, G: entries per commit group, WPB: warps per block.
-template <int SV, int S, int G, int WPB>
-__global__ void __launch_bounds__(32 * WPB) ft_segsum_stream_kernel(const SegParams p) {
-  using Ops = Vec<float4>;
-  static_assert(S % G == 0, "stages must be a multiple of the group size");
-  extern __shared__ __align__(16) unsigned char stream_smem[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float4* ring = reinterpret_cast<float4*>(stream_smem) + (warp * S * SV) * 32 + lane;
-  const int chunk = p.chunk0 + blockIdx.y;
-  const int c0 = p.g.begin(chunk);
-  const int width = p.g.width(chunk);
-  bool ok[SV];
-#pragma unroll
-  for (int v = 0; v < SV; ++v) ok[v] = lane + 32 * v < width;
-  const int w = blockIdx.x * WPB + warp;
-  if (w >= p.n_stream_warps) return;
-  const int f_begin = p.first_row[w], f_end = p.first_row[w + 1];
-  if (f_begin >= f_end) return;
-  const int64_t row_vec = p.g.n_vec;
-  const int P = p.P;
-  const int Bi = (int)p.B;
-  const float4* __restrict__ d0 = reinterpret_cast<const float4*>(p.dout[0]) + c0 + lane;
-  const float4* __restrict__ d1 = reinterpret_cast<const float4*>(P == 2 ? p.dout[1] : p.dout[0]) + c0 + lane;
-  const int E0 = p.seg_start[(int64_t)f_begin * P];
-  const int E1 = p.seg_start[(int64_t)f_end * P];
-
-  // ---- issue side: entry t -> ring slot (t - E0) % S, G entries per group
-  int t = E0, idx_base = -1, my_v = 0;
-  auto issue = [&](int slot_i) {
-    if (t < E1) {
-      const int base = t & ~31;
-      if (base != idx_base) {
-        idx_base = base;
-        my_v = base + lane < E1 ? __ldg(p.sorted_b + base + lane) : 0;
-      }
-      const int v = __shfl_sync(kFull, my_v, t & 31);
-      const int q = v >= Bi ? 1 : 0;
-      const int b = v - q * Bi;
-      const bool good = (unsigned)b < (unsigned)Bi;
-      if (!good) flag_error(kErrBadSegment);
-      const float4* src = (q ? d1 : d0) + (good ? (int64_t)b * row_vec : 0);
-#pragma unroll
-      for (int s = 0; s < SV; ++s) cp_async16_if(ring + (slot_i * SV + s) * 32, src + 32 * s, ok[s] && good);
-    }
-    ++t;
-  };
-#pragma unroll 1
-  for (int i = 0; i < S; i += G) {
-#pragma unroll
-    for (int e = 0; e < G; ++e) issue(i + e);
-    cp_async_commit();
-  }
-
-  // ---- consume side: segment boundaries of keys [f_begin * P, f_end * P]
-  int key = f_begin * P;
-  int bnd_base = -1, my_bnd = 0;
-  auto seg_end = [&](int k) {  // end of segment k = seg_start[k + 1]
-    const int idx = k + 1;
-    const int base = idx & ~31;
-    if (base != bnd_base) {
-      bnd_base = base;
-      my_bnd = p.seg_start[base + lane < p.T * P + 1 ? base + lane : p.T * P];
-    }
-    return __shfl_sync(kFull, my_bnd, idx & 31);
-  };
-  float4 acc[SV], tot[SV];
-#pragma unroll
-  for (int s = 0; s < SV; ++s) acc[s] = tot[s] = Ops::zero();
-  int end = seg_end(key);
-  int row_first = E0;
-  int j = E0, stage = 0;
-  bool done = false;
-  while (!done) {
-    cp_async_wait<S / G - 1>();  // the oldest group (G entries) has landed
-#pragma unroll
-    for (int e = 0; e < G; ++e) {
-      // close every segment that ends at j (empty segments and rows included)
-      while (!done && end == j) {
-        const int q = key - (key / P) * P;
-        if (q == 0) {
-#pragma unroll
-          for (int s = 0; s < SV; ++s) tot[s] = acc[s];
-        } else {
-#pragma unroll
-          for (int s = 0; s < SV; ++s) Ops::add(tot[s], acc[s]);
-        }
-#pragma unroll
-        for (int s = 0; s < SV; ++s) acc[s] = Ops::zero();
-        if (q == P - 1) {
-          const int64_t f = key / P;
-          seg_write<float4, SV>(p, f, c0 + lane, tot, ok, j > row_first);
-          row_first = j;
-          if (f + 1 >= f_end) done = true;
-        }
-        if (!done) {
-          ++key;
-          end = seg_end(key);
-        }
-      }
-      // a segment table that is not monotone (corrupt workspace) ends the walk
-      if (!done && (end < j || (j >= E1 && end != j))) {
-        flag_error(kErrBadSegment);
-        done = true;
-      }
-      if (!done && j < E1) {
-#pragma unroll
-        for (int s = 0; s < SV; ++s) Ops::add(acc[s], ring[((stage + e) * SV + s) * 32]);
-        ++j;
-      }
-    }
-    if (done) break;
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < G; ++e) issue(stage + e);
-    cp_async_commit();
-    stage = stage + G == S ? 0 : stage + G;
-  }
-  cp_async_wait<0>();
 }
 
 // ----------------------------------------------------------------------------

@@ -93,19 +93,13 @@ struct Tuning {
   int64_t fwd_items_per_warp = 16;  // (perspective, position) items per warp
   int64_t fwd_unroll = 6;          // table rows in flight per warp (4, 6 or 8; 5 groups: 2, 3, 4 or 6)
   int64_t bwd_unroll = 2;          // dOut rows per batch, light rows (2, 4 or 8)
-  int64_t bwd_entries_per_warp = 2048;  // streaming backward: sorted entries per warp
   int64_t fwd_min_blocks = 4;      // forward: registers sized for 2..6 resident blocks (chunks <= 64 vectors)
   int64_t bwd_min_blocks = 8;      // light rows: registers sized for 4, 5, 6 or 8 resident blocks (else compiler's)
   int64_t fwd_exact_chunks = 1;    // 1: full-width chunks + narrow tail; 0: balanced widths
   int64_t bwd_exact_chunks = 1;
-  int64_t bwd_variant = 1;  // 1: warp per light row (+ heavy-row kernel); 0: streaming
-  int64_t bwd_stream_cfg = 0;      // streaming kernel shape (stages / group / warps per block)
   int64_t bwd_chunk_vec = 32;      // backward column chunk, in 16-byte vectors
   int64_t heavy_threshold = 256;   // rows with more entries are split finer
   int64_t heavy_cap = 512;         // at most this many heavy rows per call
-  int64_t sort_tile_rows = 32;     // index rows (positions) per warp in the first sort pass
-  int64_t sort_tile = 1024;        // entries per warp in later sort passes
-  int64_t sort_variant = 1;        // 1: counting placement + per-segment sort, 0: LSD radix passes
   int64_t sort_blocks_per_sm = 16;  // counting placement: grid of the two passes over the index arrays
   int64_t colsum_parts = 296;      // position ranges of the bias column sum
   int64_t fwd_block = 128;         // forward (1 vector per lane, 4 blocks' registers): threads per block, 256 or 128
@@ -134,20 +128,14 @@ ParamRef* params() {
       {"fwd_items_per_warp", &g_tune.fwd_items_per_warp, 1, 1024},
       {"fwd_unroll", &g_tune.fwd_unroll, 2, 8},
       {"bwd_unroll", &g_tune.bwd_unroll, 2, 8},
-      {"bwd_entries_per_warp", &g_tune.bwd_entries_per_warp, 32, 1 << 24},
       {"fwd_exact_chunks", &g_tune.fwd_exact_chunks, 0, 1},
       {"bwd_exact_chunks", &g_tune.bwd_exact_chunks, 0, 1},
-      {"bwd_variant", &g_tune.bwd_variant, 0, 1},
       {"fwd_min_blocks", &g_tune.fwd_min_blocks, 0, 6},
       {"bwd_min_blocks", &g_tune.bwd_min_blocks, 0, 8},
-      {"bwd_stream_cfg", &g_tune.bwd_stream_cfg, 0, 5},
       {"bwd_chunk_vec", &g_tune.bwd_chunk_vec, 0, 1 << 20},
       {"heavy_threshold", &g_tune.heavy_threshold, 1, int64_t(1) << 40},
       {"heavy_cap", &g_tune.heavy_cap, 0, 1 << 24},
-      {"sort_tile_rows", &g_tune.sort_tile_rows, 1, 1 << 16},
-      {"sort_variant", &g_tune.sort_variant, 0, 1},
       {"sort_blocks_per_sm", &g_tune.sort_blocks_per_sm, 1, 1 << 16},
-      {"sort_tile", &g_tune.sort_tile, 32 * kSortBatch, 1 << 20},
       {"colsum_parts", &g_tune.colsum_parts, 1, 1 << 16},
       {"bwd_block", &g_tune.bwd_block, 64, 256},
       {"fwd_block", &g_tune.fwd_block, 128, 256},
@@ -346,13 +334,10 @@ int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int
 struct BwdPlan {
   int64_t B = 0, T = 0, NK = 0, nnz_max = 0;
   int32_t K = 0, C = 0, P = 0;
-  int bits = 0, npass = 0;
-  int dbits[3] = {0, 0, 0}, shift[3] = {0, 0, 0};
-  int64_t tile_raw = 0, tile = 0, tiles_raw = 0, tiles_max = 0, hist_len = 0, scan_blocks = 0;
-  int64_t heavy_cap = 0, heavy_threshold = 0, parts = 0, epw = 0, n_stream_warps = 0;
-  int sort_variant = 0;
-  size_t off_seg = 0, off_hist = 0, off_bsum = 0, off_ka = 0, off_va = 0, off_kb = 0, off_vb = 0;
-  size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, off_first = 0, off_cursor = 0, off_big = 0;
+  int64_t scan_blocks = 0;
+  int64_t heavy_cap = 0, heavy_threshold = 0, parts = 0;
+  size_t off_seg = 0, off_bsum = 0, off_ka = 0, off_va = 0;
+  size_t off_nheavy = 0, off_heavy = 0, off_kind = 0, off_partial = 0, off_cursor = 0, off_big = 0;
   size_t off_hpart = 0, off_hticket = 0;
   size_t total = 0;
 };
@@ -360,6 +345,8 @@ struct BwdPlan {
 int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl) {
   if (P != 1 && P != 2) return fail(NNUE_ERR_INVALID_ARGUMENT, "backward: n_persp must be 1 or 2");
   if (B < 0 || K < 0 || T <= 0 || C <= 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "backward: bad sizes");
+  // the segment sort counts repeats of one position in 16-bit counters
+  if (K >= 65536) return fail(NNUE_ERR_UNSUPPORTED, "backward: max_active must be < 65536");
   pl.B = B;
   pl.K = K;
   pl.T = T;
@@ -370,30 +357,10 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
     return fail(NNUE_ERR_UNSUPPORTED, "backward: num_inputs * n_persp must be < 2^30");
   pl.nnz_max = (int64_t)P * B * K;
   if (pl.nnz_max >= INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "backward: n_persp * batch * max_active >= 2^31");
-  int bits = 1;
-  while ((int64_t(1) << bits) < pl.NK) ++bits;
-  pl.bits = bits;
-  pl.npass = (int)ceil_div(bits, 10);
-  for (int i = 0, sh = 0; i < pl.npass; ++i) {
-    const int d = (int)ceil_div(bits - sh, pl.npass - i);
-    pl.dbits[i] = d;
-    pl.shift[i] = sh;
-    sh += d;
-  }
-  pl.tile_raw = g_tune.sort_tile_rows;  // rows per warp tile in the first pass
-  pl.tile = g_tune.sort_tile / (32 * kSortBatch) * (32 * kSortBatch);
-  pl.tiles_raw = pl.K > 0 ? ceil_div((int64_t)P * B, pl.tile_raw) : 0;
-  pl.tiles_max = ceil_div(pl.nnz_max, pl.tile);
-  pl.hist_len = (int64_t(1) << pl.dbits[0]) * pl.tiles_raw;
-  for (int i = 1; i < pl.npass; ++i)
-    pl.hist_len = std::max<int64_t>(pl.hist_len, (int64_t(1) << pl.dbits[i]) * pl.tiles_max);
-  pl.scan_blocks = std::max(ceil_div(pl.hist_len, kScanTile), ceil_div(pl.NK + 1, kScanTile));
+  pl.scan_blocks = ceil_div(pl.NK + 1, kScanTile);
   pl.heavy_cap = std::min<int64_t>(g_tune.heavy_cap, T);
   pl.heavy_threshold = g_tune.heavy_threshold;
   pl.parts = std::max<int64_t>(1, std::min<int64_t>(g_tune.colsum_parts, B));
-  pl.epw = g_tune.bwd_entries_per_warp;
-  pl.n_stream_warps = pl.nnz_max / pl.epw + 1;
-  pl.sort_variant = K < 65536 ? (int)g_tune.sort_variant : 0;  // 16-bit position counters
   const int64_t n_vec_floats = C;  // float64 partial column sums
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -402,19 +369,15 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
     return at;
   };
   pl.off_seg = take(sizeof(int32_t) * (pl.NK + 1));
-  pl.off_hist = take(pl.sort_variant == 1 ? 0 : sizeof(int32_t) * pl.hist_len);
   pl.off_bsum = take(sizeof(int32_t) * (pl.scan_blocks + 1));
-  pl.off_ka = take(sizeof(int32_t) * pl.nnz_max);
-  pl.off_va = take(sizeof(int32_t) * pl.nnz_max);
-  pl.off_kb = take(pl.npass >= 3 && pl.sort_variant == 0 ? sizeof(int32_t) * pl.nnz_max : 0);
-  pl.off_vb = take(pl.npass >= 2 && pl.sort_variant == 0 ? sizeof(int32_t) * pl.nnz_max : 0);
+  pl.off_ka = take(sizeof(int32_t) * pl.nnz_max);  // spare values (long-segment sort)
+  pl.off_va = take(sizeof(int32_t) * pl.nnz_max);  // the sorted values
   pl.off_nheavy = take(sizeof(int32_t));
   pl.off_heavy = take(sizeof(int32_t) * pl.heavy_cap);
   pl.off_kind = take(sizeof(uint8_t) * T);
   pl.off_partial = take(sizeof(double) * P * pl.parts * n_vec_floats);
-  pl.off_first = take(sizeof(int32_t) * (pl.n_stream_warps + 1));
-  pl.off_cursor = take(pl.sort_variant == 1 ? sizeof(int32_t) * pl.NK : 0);
-  pl.off_big = take(pl.sort_variant == 1 ? sizeof(int32_t) * (pl.NK + 1) : 0);
+  pl.off_cursor = take(sizeof(int32_t) * pl.NK);
+  pl.off_big = take(sizeof(int32_t) * (pl.NK + 1));
   pl.off_hpart = take(P == 2 ? sizeof(float) * pl.heavy_cap * 2 * C : 0);
   pl.off_hticket = take(P == 2 ? sizeof(uint32_t) * pl.heavy_cap * C : 0);
   pl.total = o;
@@ -422,10 +385,9 @@ int make_plan(int64_t B, int32_t K, int64_t T, int32_t C, int32_t P, BwdPlan& pl
 }
 
 struct Ws {
-  int32_t *seg, *hist, *bsum, *ka, *va, *kb, *vb, *nheavy, *heavy;
+  int32_t *seg, *bsum, *ka, *va, *nheavy, *heavy;
   uint8_t* kind;
   double* partial;
-  int32_t* first_row;
   int32_t *cursor, *big;
   float* hpart;
   uint32_t* hticket;
@@ -435,17 +397,13 @@ Ws carve(const BwdPlan& pl, void* base) {
   char* b = static_cast<char*>(base);
   Ws w;
   w.seg = reinterpret_cast<int32_t*>(b + pl.off_seg);
-  w.hist = reinterpret_cast<int32_t*>(b + pl.off_hist);
   w.bsum = reinterpret_cast<int32_t*>(b + pl.off_bsum);
   w.ka = reinterpret_cast<int32_t*>(b + pl.off_ka);
   w.va = reinterpret_cast<int32_t*>(b + pl.off_va);
-  w.kb = reinterpret_cast<int32_t*>(b + pl.off_kb);
-  w.vb = reinterpret_cast<int32_t*>(b + pl.off_vb);
   w.nheavy = reinterpret_cast<int32_t*>(b + pl.off_nheavy);
   w.heavy = reinterpret_cast<int32_t*>(b + pl.off_heavy);
   w.kind = reinterpret_cast<uint8_t*>(b + pl.off_kind);
   w.partial = reinterpret_cast<double*>(b + pl.off_partial);
-  w.first_row = reinterpret_cast<int32_t*>(b + pl.off_first);
   w.cursor = reinterpret_cast<int32_t*>(b + pl.off_cursor);
   w.big = reinterpret_cast<int32_t*>(b + pl.off_big);
   w.hpart = reinterpret_cast<float*>(b + pl.off_hpart);
@@ -453,10 +411,8 @@ Ws carve(const BwdPlan& pl, void* base) {
   return w;
 }
 
-// sorted position list = values written by the last pass
-const int32_t* sorted_values(const BwdPlan& pl, const Ws& w) {
-  return (pl.sort_variant == 1 || pl.npass % 2 == 1) ? w.va : w.vb;
-}
+// the sorted position lists (grouped by key, ascending within a key)
+const int32_t* sorted_values(const BwdPlan&, const Ws& w) { return w.va; }
 
 void run_scan(int32_t* data, ScanLen L, int64_t max_len, int32_t* bsum, cudaStream_t s) {
   const int64_t nb = ceil_div(max_len, kScanTile);
@@ -480,74 +436,25 @@ int prepare_impl(const int32_t* idx0, const int32_t* idx1, const BwdPlan& pl, co
   raw.K = pl.K;
   raw.T = (int32_t)pl.T;
   raw.P = pl.P;
-  if (pl.sort_variant == 1) {
-    if (cudaMemsetAsync(w.big, 0, sizeof(int32_t), s) != cudaSuccess)
-      return check_launch("backward_prepare: memset");
-    const unsigned grid = (unsigned)std::max<int64_t>(
-        1, std::min<int64_t>(ceil_div(raw.n_raw, 4 * kBlock), 148 * g_tune.sort_blocks_per_sm));
-    count_launch();
-    count_keys_kernel<<<grid, kBlock, 0, s>>>(raw, w.seg);
-    run_scan(w.seg, ScanLen{pl.NK + 1, nullptr, 0, 0}, pl.NK + 1, w.bsum, s);
-    if (cudaMemcpyAsync(w.cursor, w.seg, sizeof(int32_t) * pl.NK, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-      return check_launch("backward_prepare: cursor copy");
-    count_launch();
-    place_keys_kernel<<<grid, kBlock, 0, s>>>(raw, w.cursor, w.va, pl.nnz_max);
-    count_launch();
-    order_segments_kernel<<<(unsigned)ceil_div(pl.NK, kWarpsPerBlock), kBlock, 0, s>>>(w.seg, pl.NK, w.va, w.big);
-    count_launch();
-    order_big_segments_kernel<<<(unsigned)std::min<int64_t>(pl.NK, 2 * 148), kBigThreads, 0, s>>>(
-        w.seg, pl.P, pl.B, w.va, w.ka, w.big);
-  }
-  for (int i = 0; i < (pl.sort_variant == 1 ? 0 : pl.npass); ++i) {
-    const bool first = i == 0, last = i == pl.npass - 1;
-    PassParams pp{};
-    pp.raw = raw;
-    pp.count = w.seg + pl.NK;  // number of valid entries, known after pass 0's scan
-    pp.shift = pl.shift[i];
-    pp.bits = pl.dbits[i];
-    pp.tile = (int32_t)(first ? pl.tile_raw : pl.tile);
-    pp.tile_hist = w.hist;
-    pp.key_count = first ? w.seg : nullptr;
-    // ping-pong: pass 0 -> A, pass 1 -> B, pass 2 -> A
-    int32_t* ok_ = (i % 2 == 0) ? w.ka : w.kb;
-    int32_t* ov_ = (i % 2 == 0) ? w.va : w.vb;
-    pp.in_keys = (i % 2 == 1) ? w.ka : w.kb;
-    pp.in_vals = (i % 2 == 1) ? w.va : w.vb;
-    pp.out_keys = last ? nullptr : ok_;
-    pp.out_vals = ov_;
-    pp.out_cap = pl.nnz_max;
-    const int bins = 1 << pl.dbits[i];
-    const size_t smem = sizeof(int32_t) * bins * kWarpsPerBlock;
-    const int64_t tiles = first ? pl.tiles_raw : pl.tiles_max;
-    if (tiles == 0) continue;
-    const unsigned grid = (unsigned)ceil_div(tiles, kWarpsPerBlock);
-    if (first) {
-      count_launch();
-      sort_hist_rows_kernel<<<grid, kBlock, smem, s>>>(pp);
-      run_scan(w.hist, ScanLen{bins * tiles, nullptr, 0, 0}, bins * tiles, w.bsum, s);
-      run_scan(w.seg, ScanLen{pl.NK + 1, nullptr, 0, 0}, pl.NK + 1, w.bsum, s);
-      count_launch();
-      sort_scatter_rows_kernel<<<grid, kBlock, smem, s>>>(pp);
-    } else {
-      count_launch();
-      sort_hist_kernel<<<grid, kBlock, smem, s>>>(pp);
-      run_scan(w.hist, ScanLen{0, pp.count, pp.tile, bins}, (int64_t)bins * tiles, w.bsum, s);
-      count_launch();
-      sort_scatter_kernel<<<grid, kBlock, smem, s>>>(pp);
-    }
-  }
-  if (pl.nnz_max == 0) {
-    // no entries: seg is all zero already (memset); nothing else to do
-  }
+  if (cudaMemsetAsync(w.big, 0, sizeof(int32_t), s) != cudaSuccess) return check_launch("backward_prepare: memset");
+  const unsigned grid = (unsigned)std::max<int64_t>(
+      1, std::min<int64_t>(ceil_div(raw.n_raw, 4 * kBlock), 148 * g_tune.sort_blocks_per_sm));
+  count_launch();
+  count_keys_kernel<<<grid, kBlock, 0, s>>>(raw, w.seg);
+  run_scan(w.seg, ScanLen{pl.NK + 1}, pl.NK + 1, w.bsum, s);
+  if (cudaMemcpyAsync(w.cursor, w.seg, sizeof(int32_t) * pl.NK, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("backward_prepare: cursor copy");
+  count_launch();
+  place_keys_kernel<<<grid, kBlock, 0, s>>>(raw, w.cursor, w.va, pl.nnz_max);
+  count_launch();
+  order_segments_kernel<<<(unsigned)ceil_div(pl.NK, kWarpsPerBlock), kBlock, 0, s>>>(w.seg, pl.NK, w.va, w.big);
+  count_launch();
+  order_big_segments_kernel<<<(unsigned)std::min<int64_t>(pl.NK, 2 * 148), kBigThreads, 0, s>>>(
+      w.seg, pl.P, pl.B, w.va, w.ka, w.big);
   count_launch();
   classify_rows_kernel<<<(unsigned)ceil_div(pl.T, kBlock), kBlock, 0, s>>>(
       w.seg, (int32_t)pl.T, pl.P, (int32_t)std::min<int64_t>(pl.heavy_threshold, INT32_MAX),
       (int32_t)pl.heavy_cap, w.nheavy, w.heavy, w.kind);
-  if (g_tune.bwd_variant == 0) {  // only the streaming apply uses the per-warp row ranges
-    count_launch();
-    warp_ranges_kernel<<<(unsigned)ceil_div(pl.T + 1, kBlock), kBlock, 0, s>>>(
-        w.seg, (int32_t)pl.T, pl.P, (int32_t)pl.epw, (int32_t)pl.n_stream_warps, w.first_row);
-  }
   return check_launch("backward_prepare");
 }
 
@@ -743,38 +650,6 @@ void launch_colsum(const float* g0, const float* g1, const BwdPlan& pl, bool vec
                                                                                  pl.C, dB, accumulate);
 }
 
-template <int SV, int S, int G, int WPB>
-int launch_segsum_stream_cfg(SegParams p, cudaStream_t s) {
-  constexpr size_t smem = sizeof(float4) * 32 * SV * S * WPB;
-  static std::atomic<unsigned long long> attr_set_mask{0};  // one bit per device
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("backward_apply: device");
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (smem > 48 * 1024 && !(attr_set_mask.load() & bit)) {
-    if (cudaFuncSetAttribute(ft_segsum_stream_kernel<SV, S, G, WPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return check_launch("backward_apply: stream kernel shared memory");
-    attr_set_mask.fetch_or(bit);
-  }
-  p.chunk0 = 0;
-  dim3 grid((unsigned)ceil_div(p.n_stream_warps, WPB), (unsigned)p.g.n_chunks);
-  count_launch();
-  ft_segsum_stream_kernel<SV, S, G, WPB><<<grid, 32 * WPB, smem, s>>>(p);
-  return NNUE_OK;
-}
-
-template <int SV>
-int launch_segsum_stream(const SegParams& p, cudaStream_t s) {
-  switch (g_tune.bwd_stream_cfg) {
-    case 0: return launch_segsum_stream_cfg<SV, 16, 4, 4>(p, s);
-    case 1: return launch_segsum_stream_cfg<SV, 16, 4, 8>(p, s);
-    case 2: return launch_segsum_stream_cfg<SV, 8, 2, 8>(p, s);
-    case 3: return launch_segsum_stream_cfg<SV, 32, 4, 4>(p, s);
-    case 4: return launch_segsum_stream_cfg<SV, 16, 1, 4>(p, s);
-    default: return launch_segsum_stream_cfg<SV, 8, 4, 8>(p, s);
-  }
-}
-
 int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w, float* dW, float* dB,
                int32_t accumulate, int64_t row_begin, int64_t row_end, bool with_bias, cudaStream_t s,
                const TableSet* dws = nullptr) {
@@ -799,8 +674,6 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   p.P = pl.P;
   p.accumulate = accumulate ? 1 : 0;
   p.heavy_cap = (int32_t)pl.heavy_cap;
-  p.first_row = w.first_row;
-  p.n_stream_warps = (int32_t)pl.n_stream_warps;
   p.row_begin = (int32_t)row_begin;
   p.row_end = (int32_t)row_end;
   if (dws && dws->n > 1) p.dws = *dws;
@@ -833,18 +706,16 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     }
   }
 
-  const bool full_range = row_begin == 0 && row_end == pl.T;
-  const bool stream = v4 && g_tune.bwd_variant == 0 && lanes_per_row(p.g) <= 2 && full_range;
   const bool rows = row_end > row_begin;
   DeviceAux* aux = nullptr;
   int rc = device_aux(&aux);
   if (rc != NNUE_OK) return rc;
   {
-    // fork: (fallback path: heavy rows +) bias column sum on the side stream
+    // fork: heavy rows and the bias column sum on the side stream
     std::lock_guard<std::mutex> lock(g_aux_mu);
     if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
       return check_launch("backward_apply: fork");
-    if (!stream && rows) {
+    if (rows) {
       if (pl.P == 2 && pl.heavy_cap > 0 &&
           cudaMemsetAsync(w.hticket, 0, sizeof(uint32_t) * pl.heavy_cap * p.g.n_vec, aux->side) != cudaSuccess)
         return check_launch("backward_apply: heavy tickets");
@@ -854,10 +725,7 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     if (with_bias) launch_colsum(g0, g1, pl, v4, w.partial, dB, p.accumulate, aux->side);
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
   }
-  if (stream) {
-    rc = lanes_per_row(p.g) == 1 ? launch_segsum_stream<1>(p, s) : launch_segsum_stream<2>(p, s);
-    if (rc != NNUE_OK) return rc;
-  } else if (rows && v4) {
+  if (rows && v4) {
     launch_segsum_light<float4>(p, queue_ok, s);
   } else if (rows) {
     launch_segsum_light<float>(p, false, s);

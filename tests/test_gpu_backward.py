@@ -21,16 +21,6 @@ pytestmark = pytest.mark.gpu
 RTOL, ATOL = 1e-5, 1e-6
 
 
-@pytest.fixture(autouse=True, params=[0, 1], ids=["radix", "counting"])
-def sort_variant(request):
-    """Every test runs with both index phases: LSD radix passes, and counting
-    placement + per-segment sort."""
-    old = _native.get_param("sort_variant")
-    _native.set_param("sort_variant", request.param)
-    yield request.param
-    _native.set_param("sort_variant", old)
-
-
 def _grads(B, C, seed):
     rng = np.random.default_rng(seed)
     return rng.standard_normal((B, C), dtype=np.float32), rng.standard_normal((B, C), dtype=np.float32)
@@ -94,13 +84,10 @@ def _with_params(params, fn):
 @pytest.mark.parametrize(
     "params",
     [
-        {"bwd_variant": 1, "heavy_threshold": 4, "heavy_cap": 3},  # heavy rows overflow to the light path
-        {"bwd_variant": 1, "heavy_threshold": 1, "heavy_cap": 100000},  # nearly every row heavy
-        {"bwd_variant": 1, "heavy_threshold": 10**9},  # no heavy rows
-        {"bwd_variant": 1},
-        {"bwd_entries_per_warp": 32},
-        {"bwd_entries_per_warp": 100},
-        {"bwd_entries_per_warp": 5000},
+        {"heavy_threshold": 4, "heavy_cap": 3},  # heavy rows overflow to the light path
+        {"heavy_threshold": 1, "heavy_cap": 100000},  # nearly every row heavy
+        {"heavy_threshold": 10**9},  # no heavy rows
+        {},
         {"bwd_exact_chunks": 1},
         {"bwd_chunk_vec": 64, "bwd_exact_chunks": 1},
         {"bwd_chunk_vec": 8},
@@ -108,8 +95,8 @@ def _with_params(params, fn):
         {"bwd_chunk_vec": 32},
         {"bwd_chunk_vec": 128},
         {"bwd_chunk_vec": 1000},
-        {"sort_tile_rows": 1, "sort_tile": 512},
-        {"sort_tile_rows": 7, "sort_tile": 1536},
+        {"sort_blocks_per_sm": 1},
+        {"sort_blocks_per_sm": 64},
         {"colsum_parts": 1},
         {"bwd_queue": 0, "bwd_unroll": 2, "bwd_min_blocks": 8},
         {"bwd_queue": 0, "bwd_unroll": 8, "bwd_min_blocks": 4},
@@ -171,8 +158,8 @@ def test_backward_misaligned_gradients_use_scalar_path(cuda):
     np.testing.assert_allclose(dB.cpu().numpy(), rB, rtol=RTOL, atol=ATOL)
 
 
-def test_backward_radix_pass_counts(cuda):
-    # T * P <= 1024 -> one digit pass; >= 2^20 -> three passes
+def test_backward_small_and_large_key_spaces(cuda):
+    # T * P keys from 200 to 1.2 M: one scan block to many
     for T, C in ((100, 8), (600_000, 4)):
         B, K = 1200, 9
         i0 = random_indices(B, K, T, seed=T % 97)
@@ -287,3 +274,10 @@ def test_backward_gradients_in_reverse_memory_order(cuda, queue):
     rW, rB = oracle.ft_backward_pair(white, black, g0.cpu().numpy(), g1.cpu().numpy(), T)
     np.testing.assert_array_equal(dW.cpu().numpy(), rW)
     np.testing.assert_allclose(dB.cpu().numpy(), rB, rtol=RTOL, atol=ATOL)
+
+
+def test_backward_rejects_max_active_beyond_counters(cuda):
+    """The per-segment sort counts repeats of a position in 16-bit counters,
+    so max_active >= 65536 is refused instead of mis-sorted."""
+    lib = _native.load()
+    assert lib.nnue_ft_backward_workspace_size(4, 65536, 100, 8, 2) == 0

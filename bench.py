@@ -126,6 +126,21 @@ def captured_traffic():
     return cap
 
 
+def timed_kernel_columns(C: int, tail_knob: int, items: int, forward: bool) -> int:
+    """Columns (floats) the timed main gather kernel covers.  The library
+    packs a narrow last column chunk (2, 3, 4, 6 or 8 of the row's 16-byte
+    vectors past full 32-vector chunks) into a kernel of its own when the
+    tail knob is on (forward mode 3: only from 2^17 items); that kernel is
+    not timed with the main one."""
+    n_vec, tail = C // 4, (C // 4) % 32
+    if C % 4 or n_vec < 64 or tail not in (2, 3, 4, 6, 8):
+        return C
+    mode = tail_knob
+    if forward and mode == 3:
+        mode = 2 if items >= (1 << 17) else 0
+    return C if mode == 0 else (n_vec - tail) * 4
+
+
 def hbm_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -556,12 +571,17 @@ def run_ours(args):
     #            light row of dW written once;
     #   heavy rows: the same for the heavy rows.
     peak, peak_src = hbm_peak()
+    # With the narrow last column chunk packed into its own kernel on the side
+    # stream, the timed forward / light-row kernels cover the other columns
+    # only: count the bytes of the columns each timed kernel covers.
+    c_fwd = timed_kernel_columns(C, _native.get_param("fwd_tail"), 2 * b_rank, forward=True)
+    c_light = timed_kernel_columns(C, _native.get_param("bwd_tail"), 2 * b_rank, forward=False)
     counts = np.bincount(white[white >= 0], minlength=T) + np.bincount(black[black >= 0], minlength=T)
     heavy = np.sort(counts[counts > _native.get_param("heavy_threshold")])[::-1][:_native.get_param("heavy_cap")]
     n_heavy, nnz_heavy = int(heavy.size), int(heavy.sum())
     nnz_light = nnz_rank - nnz_heavy
-    a_fwd = nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4 + C * 4
-    a_light = nnz_light * (C * 4 + 4) + (2 * T + 1) * 4 + T + (T - n_heavy) * C * 4
+    a_fwd = nnz_rank * c_fwd * 4 + 2 * b_rank * c_fwd * 4 + 2 * b_rank * K * 4 + c_fwd * 4
+    a_light = nnz_light * (c_light * 4 + 4) + (2 * T + 1) * 4 + T + (T - n_heavy) * c_light * 4
     a_heavy = nnz_heavy * (C * 4 + 4) + n_heavy * C * 4
     a_step_survey = (nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4) + \
                     (nnz_rank * C * 4 + 2 * b_rank * K * 4 + T * C * 4)

@@ -745,6 +745,119 @@ __global__ void __launch_bounds__(BLOCK, MINB) ft_segsum_lightq_kernel(const Seg
   seg_write<float4, 1>(p, f, col, tot, okv, n > 0);
 }
 
+// Light rows, the narrow last column chunk (W <= 8 vectors; 6 for C = 1048),
+// packed: G = 32 / W consecutive rows per warp, lane group g (lanes g*W ..
+// g*W + W - 1) owning row f0 + g and the chunk's W columns.  A full-width
+// warp on this chunk would keep 32 - W lanes idle through a whole row walk.
+// The G rows' entries are contiguous in sorted_b, so one warp-wide pass turns
+// them into row offsets in a shared-memory list (a value's perspective is
+// v >= B); then all groups walk their perspective-0 entries in lockstep
+// through a D-slot register queue, then their perspective-1 entries, and
+// write dW = acc0 + acc1 -- each column summed in ascending b per
+// perspective, the same adds as ft_segsum_lightq_kernel.  A warp whose rows
+// hold more than kTailList entries, or one of which is heavy, walks its rows
+// straight from sorted_b instead (rare: only the 32 own-king rows are heavy).
+constexpr int kTailList = 1280;
+
+template <int W, int D>
+__global__ void __launch_bounds__(128, 8) ft_segsum_tail_kernel(const SegParams p) {
+  using Ops = Vec<float4>;
+  // G rows need G * P + 1 segment bounds, one per lane: at most 15 rows
+  constexpr int G = 32 / W < 15 ? 32 / W : 15;
+  __shared__ int s_list[4][kTailList];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int* list = s_list[warp];
+  const int g = lane / W, sub = lane - g * W;
+  const bool live_lane = g < G;
+  const int P = p.P;
+  const int chunk = p.g.n_chunks - 1;
+  const int col = p.g.begin(chunk) + sub;
+  const int row_vec = p.g.n_vec;
+  const int B = (int)p.B;
+  const int64_t f0 = p.row_begin + ((int64_t)blockIdx.x * 4 + warp) * G;
+  if (f0 >= p.row_end) return;
+  const int n_rows = p.row_end - f0 < G ? (int)(p.row_end - f0) : G;
+  // segment bounds of the G rows (G * P + 1 values) and their kinds
+  const int bnd = lane <= n_rows * P ? p.seg_start[f0 * P + lane] : 0;
+  const int kind = lane < n_rows ? p.row_kind[f0 + lane] : 0;
+  const bool row_live = live_lane && g < n_rows;
+  const int gg = row_live ? g : 0;
+  const int s0 = __shfl_sync(kFull, bnd, gg * P);
+  const int s1 = __shfl_sync(kFull, bnd, gg * P + 1);  // P == 1: the row's end
+  const int e1 = __shfl_sync(kFull, bnd, (gg + 1) * P);
+  const int my_kind = __shfl_sync(kFull, kind, gg);
+  const int S = __shfl_sync(kFull, bnd, 0);
+  const int E = __shfl_sync(kFull, bnd, n_rows * P);
+  const bool any_heavy = __any_sync(kFull, lane < n_rows && kind != 0);
+  // bounds must nest (S <= s0 <= s1 <= e1 <= E); a corrupt workspace is
+  // flagged and its row left empty, so no walk leaves the written list
+  const bool sane = S <= s0 && s0 <= s1 && s1 <= e1 && e1 <= E;
+  if (row_live && !my_kind && !sane) flag_error(kErrBadSegment);
+  const bool walk_row = row_live && !my_kind && sane;
+  const int n0 = walk_row ? s1 - s0 : 0;
+  const int n1 = walk_row && P == 2 ? e1 - s1 : 0;
+  const float4* __restrict__ src = reinterpret_cast<const float4*>(p.dout[0]) + col;
+  float4 acc0 = Ops::zero(), acc1 = Ops::zero();
+  if (!any_heavy && E - S <= kTailList) {
+    for (int e = lane; e < E - S; e += 32) {
+      const int v = __ldg(p.sorted_b + S + e);
+      const bool q = v >= B;
+      int b = v - (q ? B : 0);
+      if ((unsigned)b >= (unsigned)B) {  // corrupt workspace: flag, read row 0
+        flag_error(kErrBadSegment);
+        b = 0;
+      }
+      list[e] = b * row_vec + (q ? p.persp_delta : 0);
+    }
+    __syncwarp();
+    // each group walks list[at, at + n) with the queue; all groups in lockstep
+    auto walk = [&](int at, int n, float4& acc) {
+      int n_max = n;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const int t = __shfl_xor_sync(kFull, n_max, o);
+        n_max = t > n_max ? t : n_max;
+      }
+      float4 w[D];
+#pragma unroll
+      for (int d = 0; d < D; ++d)
+        if (d < n) w[d] = Ops::ldg(src + list[at + d]);
+      for (int j0 = 0; j0 < n_max; j0 += D) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+          const int j = j0 + d;
+          if (j < n) {
+            Ops::add(acc, w[d]);
+            if (j + D < n) w[d] = Ops::ldg(src + list[at + j + D]);
+          }
+        }
+      }
+    };
+    walk(s0 - S, n0, acc0);
+    if (P == 2) walk(s1 - S, n1, acc1);
+  } else {
+    // entry by entry from sorted_b (a heavy row among the G, or a very long row)
+    for (int j = 0; j < n0 + n1; ++j) {
+      const int v = __ldg(p.sorted_b + s0 + j);
+      const bool q = j >= n0;
+      int b = v - (q ? B : 0);
+      if ((unsigned)b >= (unsigned)B) {
+        flag_error(kErrBadSegment);
+        b = 0;
+      }
+      const float4 x = Ops::ldg(src + (b * row_vec + (q ? p.persp_delta : 0)));
+      if (q) Ops::add(acc1, x);
+      else Ops::add(acc0, x);
+    }
+  }
+  if (row_live && !my_kind) {
+    float4 tot[1] = {acc0};
+    if (P == 2) Ops::add(tot[0], acc1);
+    const bool okv[1] = {true};
+    seg_write<float4, 1>(p, f0 + g, col, tot, okv, n0 + n1 > 0);
+  }
+}
+
 // Heavy rows: a long sum per column whose only order-preserving parallelism
 // is across columns and across the two perspectives.  One warp per (row,
 // 32-vector piece of a column chunk, perspective) streams the segment's dOut

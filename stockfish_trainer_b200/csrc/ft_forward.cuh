@@ -192,6 +192,82 @@ __global__ void __launch_bounds__(BLOCK, MINB) ft_forward_kernel(const FwdParams
   }
 }
 
+// The narrow last column chunk (W <= 16 vectors; 6 for C = 1048), packed:
+// G = 32 / W items at once per warp, lane group g (lanes g*W .. g*W + W - 1)
+// owning item `base + g` and the chunk's W columns.  A full-width warp on this
+// chunk would keep 32 - W lanes idle through a whole item walk -- one ninth
+// of the kernel's warp time for a fiftieth of its bytes.  The G items'
+// valid indices are compacted one item at a time (whole-warp ballots) into
+// per-group shared-memory lists, then every group walks its own list
+// through a D-slot register queue, all groups in lockstep up to the longest
+// list.  Each lane still sums its column bias-first then in ascending k, so
+// the outputs equal ft_forward_kernel's bit for bit.  Needs K <= 32 * IG
+// (one index pass per item).
+template <int W, int D, int IG, int MINB, int BLOCK>
+__global__ void __launch_bounds__(BLOCK, MINB) ft_forward_tail_kernel(const FwdParams p) {
+  using Ops = Vec<float4>;
+  constexpr int G = 32 / W;
+  constexpr int kStride = 32 * IG + 1;  // +1: the groups' lists start in different banks
+  __shared__ int s_list[BLOCK / 32][G * kStride];
+  const int lane = threadIdx.x & 31;
+  int* lists = s_list[threadIdx.x >> 5];
+  const int g = lane / W, sub = lane - g * W;
+  const bool live = g < G;
+  const int chunk = p.g.n_chunks - 1;
+  const int c0 = p.g.begin(chunk);
+  const int row_vec = p.g.n_vec;
+  const float4* __restrict__ Wv = reinterpret_cast<const float4*>(p.W) + c0 + sub;
+  const float4 bvec = live ? Ops::ldg(reinterpret_cast<const float4*>(p.bias) + c0 + sub) : Ops::zero();
+  int* my_list = lists + (live ? g : 0) * kStride;
+
+  const int64_t n_items = (int64_t)p.P * p.B;
+  int64_t item = ((int64_t)blockIdx.x * (BLOCK / 32) + (threadIdx.x >> 5)) * (int64_t)p.items_per_warp * G;
+  const int64_t item_end =
+      item + (int64_t)p.items_per_warp * G < n_items ? item + (int64_t)p.items_per_warp * G : n_items;
+  auto index_row = [&](int64_t it) {
+    const int q = it >= p.B ? 1 : 0;
+    return (q ? p.idx[1] : p.idx[0]) + (it - (int64_t)q * p.B) * p.K;
+  };
+  for (; item < item_end; item += G) {
+    // compaction: item base + t into list t
+    int n_mine = 0, n_max = 0;
+#pragma unroll 1
+    for (int t = 0; t < G; ++t) {
+      int n_t = 0;
+      if (item + t < item_end) {
+        int f[IG];
+        load_index_groups<IG>(index_row(item + t), p.K, 0, lane, f);
+        n_t = compact_valid<IG>(f, p.T, lists + t * kStride, lane, row_vec);
+      }
+      if (t == g) n_mine = n_t;
+      n_max = n_t > n_max ? n_t : n_max;
+    }
+    if (!live) n_mine = 0;
+    float4 acc = bvec;
+    float4 w[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      if (d < n_mine) w[d] = Ops::ldg(Wv + my_list[d]);
+    for (int j0 = 0; j0 < n_max; j0 += D) {
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+        const int j = j0 + d;
+        if (j < n_mine) {
+          Ops::add(acc, w[d]);
+          if (j + D < n_mine) w[d] = Ops::ldg(Wv + my_list[j + D]);
+        }
+      }
+    }
+    const int64_t it = item + g;
+    if (live && it < item_end) {
+      const int persp = it >= p.B ? 1 : 0;
+      const int64_t b = it - (int64_t)persp * p.B;
+      Ops::st_stream(reinterpret_cast<float4*>(persp ? p.out[1] : p.out[0]) + b * row_vec + c0 + sub, acc);
+    }
+    __syncwarp();  // every lane has read the lists before they are rewritten
+  }
+}
+
 // out[r] = weight[r] + virtual_weight[r % period], one fp32 add per element:
 // HalfKav2Hm.merged_weight (halfka_v2_hm.py:69-70, weight +
 // virtual_weight.repeat(NUM_BUCKETS, 1)) without materialising the repeat.

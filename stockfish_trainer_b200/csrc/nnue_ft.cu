@@ -113,6 +113,13 @@ struct Tuning {
   // (1 for K <= 32, 5 for K <= 160): on B200 5 groups instead of 8 made the K = 160 forward 4% faster
   int64_t fwd_groups = 0;
   int64_t fwd_queue_blocks = 8;    // forward with 1 or 5 groups: register budget for 8, 12 or 16 resident 128-thread blocks
+  // the narrow last column chunk packed several items (forward) / rows (light rows) per warp: 0 off, 1 on the
+  // caller's stream, 2 on the library's side stream beside the main kernel (where the call forks one), 3 (forward
+  // only) as 2 from 2^17 items (both perspectives) up, else off.  On B200 the packed light-row tail on the side
+  // stream made the step 2-4% faster at every size; the forward's only at the largest batches (1.5% at 2 x 65536
+  // items, 1.5% slower at 2 x 8192).
+  int64_t fwd_tail = 3;
+  int64_t bwd_tail = 2;
 };
 Tuning g_tune;
 
@@ -144,6 +151,8 @@ ParamRef* params() {
       {"bwd_queue_min_entries", &g_tune.bwd_queue_min_entries, 0, int64_t(1) << 40},
       {"fwd_groups", &g_tune.fwd_groups, 0, 8},
       {"fwd_queue_blocks", &g_tune.fwd_queue_blocks, 8, 16},
+      {"fwd_tail", &g_tune.fwd_tail, 0, 3},
+      {"bwd_tail", &g_tune.bwd_tail, 0, 2},
       {nullptr, nullptr, 0, 0},
   };
   return p;
@@ -260,10 +269,53 @@ void launch_forward_range(const FwdParams& p, int chunk0, int n_chunks, int widt
   }
 }
 
+// The packed narrow last chunk (ft_forward_tail_kernel): W = the tail's width.
+template <int W, int IG>
+void launch_forward_tail_w(FwdParams p, cudaStream_t s) {
+  constexpr int G = 32 / W;
+  p.items_per_warp = 1;  // one packed group of G items per warp: enough warps at small batches
+  const int64_t n_items = (int64_t)p.P * p.B;
+  const int64_t warps = ceil_div(n_items, (int64_t)p.items_per_warp * G);
+  count_launch();
+  ft_forward_tail_kernel<W, 6, IG, 8, 128><<<(unsigned)ceil_div(warps, 4), 128, 0, s>>>(p);
+}
+
+template <int IG>
+bool launch_forward_tail_ig(const FwdParams& p, int width, cudaStream_t s) {
+  switch (width) {
+    case 2: launch_forward_tail_w<2, IG>(p, s); return true;
+    case 3: launch_forward_tail_w<3, IG>(p, s); return true;
+    case 4: launch_forward_tail_w<4, IG>(p, s); return true;
+    case 6: launch_forward_tail_w<6, IG>(p, s); return true;
+    case 8: launch_forward_tail_w<8, IG>(p, s); return true;
+    default: return false;
+  }
+}
+
+// Launches the packed tail kernel for the last column chunk when it applies
+// (16-byte vectors, one table, full-width chunks + a narrow tail, K covered by
+// one index pass); returns whether it did.
 template <typename VT>
-void launch_forward(const FwdParams& p, cudaStream_t s) {
+bool launch_forward_tail(const FwdParams& p, cudaStream_t s) {
+  if (!std::is_same<VT, float4>::value || !p.g.exact || p.g.n_chunks < 2 || p.tabs.n > 1) return false;
+  const int width = p.g.width(p.g.n_chunks - 1);
+  if (width >= p.g.max_width || width > 8 || p.g.max_width > 32) return false;
+  if (p.K <= 32) return launch_forward_tail_ig<1>(p, width, s);
+  if (p.K <= 160) return launch_forward_tail_ig<5>(p, width, s);
+  return false;
+}
+
+// fwd_tail: 0 the last chunk like the others; 1 packed, on the caller's
+// stream before the main gather; 2 packed, on the forked side stream when
+// there is one (beside the main gather), else as 1; 3 as 2 for large batches.
+template <typename VT>
+void launch_forward(const FwdParams& p, cudaStream_t s, cudaStream_t side) {
   const int slot = timer_begin(kTimeForward, s);
-  launch_forward_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
+  int64_t mode = g_tune.fwd_tail;
+  if (mode == 3) mode = (int64_t)p.P * p.B >= (int64_t(1) << 17) ? 2 : 0;
+  bool packed = false;
+  if (mode) packed = launch_forward_tail<VT>(p, mode == 2 && side ? side : s);
+  launch_forward_range<VT>(p, 0, p.g.n_chunks - (packed ? 1 : 0), p.g.max_width, s);
   timer_end(slot, s);
 }
 
@@ -293,9 +345,11 @@ bool tables_aligned16(const TableSet& t) {
   return true;
 }
 
+// `side`: a stream already forked from `s` (joined back by the caller), or
+// null; the packed tail chunk may run there, beside the main gather.
 int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int32_t K, const float* W,
                  int64_t T, int32_t C, const float* bias, float* out0, float* out1, cudaStream_t s,
-                 const TableSet* tabs = nullptr) {
+                 const TableSet* tabs = nullptr, cudaStream_t side = nullptr) {
   if (B < 0 || K < 0 || T < 0 || C <= 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "forward: bad sizes");
   if (T > INT32_MAX) return fail(NNUE_ERR_UNSUPPORTED, "forward: num_inputs exceeds int32 index range");
   if (B == 0) return NNUE_OK;
@@ -323,8 +377,8 @@ int forward_impl(const int32_t* idx0, const int32_t* idx1, int P, int64_t B, int
   if (lanes_per_row(p.g) > kMaxLaneVectors) return fail(NNUE_ERR_UNSUPPORTED, "forward: column chunk too wide");
   if (T * (int64_t)p.g.n_vec > INT32_MAX)
     return fail(NNUE_ERR_UNSUPPORTED, "forward: table exceeds 2^31 %s", v4 ? "16-byte vectors" : "floats");
-  if (v4) launch_forward<float4>(p, s);
-  else launch_forward<float>(p, s);
+  if (v4) launch_forward<float4>(p, s, side);
+  else launch_forward<float>(p, s, side);
   return check_launch("forward");
 }
 
@@ -515,46 +569,76 @@ void launch_segsum_range(const SegParams& p, int chunk0, int n_chunks, int width
 }
 
 template <int D, int MINB, int THREADS = 128>
-void launch_segsum_queue_d(const SegParams& p, cudaStream_t s) {
+void launch_segsum_queue_d(SegParams p, int n_chunks, cudaStream_t s) {
   const int64_t rows = p.row_end - p.row_begin;
+  p.chunk0 = 0;
   count_launch();
   ft_segsum_lightq_kernel<D, MINB, THREADS>
-      <<<dim3((unsigned)ceil_div(rows, THREADS / 32), (unsigned)p.g.n_chunks), THREADS, 0, s>>>(p);
+      <<<dim3((unsigned)ceil_div(rows, THREADS / 32), (unsigned)n_chunks), THREADS, 0, s>>>(p);
 }
 
-// Queued light rows (one vector per lane): depth x register budget (x block
-// size: 128 threads, or 64 with 32 resident blocks).
-bool launch_segsum_queue(const SegParams& p, cudaStream_t s) {
+// Queued light rows (one vector per lane) over column chunks [0, n_chunks):
+// depth x register budget (x block size: 128 threads, or 64 with 32 resident
+// blocks).
+bool launch_segsum_queue(const SegParams& p, int n_chunks, cudaStream_t s) {
   const int64_t mb = g_tune.bwd_queue_min_blocks;
   if (g_tune.bwd_block == 64 && mb >= 16 && (g_tune.bwd_queue == 2 || g_tune.bwd_queue == 3)) {
-    if (g_tune.bwd_queue == 2) launch_segsum_queue_d<2, 32, 64>(p, s);
-    else launch_segsum_queue_d<3, 32, 64>(p, s);
+    if (g_tune.bwd_queue == 2) launch_segsum_queue_d<2, 32, 64>(p, n_chunks, s);
+    else launch_segsum_queue_d<3, 32, 64>(p, n_chunks, s);
     return true;
   }
   switch (g_tune.bwd_queue) {
-    case 2: launch_segsum_queue_d<2, 16>(p, s); return true;
+    case 2: launch_segsum_queue_d<2, 16>(p, n_chunks, s); return true;
     case 3:
-      if (mb >= 16) launch_segsum_queue_d<3, 16>(p, s);
-      else launch_segsum_queue_d<3, 12>(p, s);
+      if (mb >= 16) launch_segsum_queue_d<3, 16>(p, n_chunks, s);
+      else launch_segsum_queue_d<3, 12>(p, n_chunks, s);
       return true;
     case 4:
-      if (mb >= 16) launch_segsum_queue_d<4, 16>(p, s);
-      else if (mb >= 12) launch_segsum_queue_d<4, 12>(p, s);
-      else launch_segsum_queue_d<4, 8>(p, s);
+      if (mb >= 16) launch_segsum_queue_d<4, 16>(p, n_chunks, s);
+      else if (mb >= 12) launch_segsum_queue_d<4, 12>(p, n_chunks, s);
+      else launch_segsum_queue_d<4, 8>(p, n_chunks, s);
       return true;
     case 6:
-      if (mb >= 12) launch_segsum_queue_d<6, 12>(p, s);
-      else launch_segsum_queue_d<6, 8>(p, s);
+      if (mb >= 12) launch_segsum_queue_d<6, 12>(p, n_chunks, s);
+      else launch_segsum_queue_d<6, 8>(p, n_chunks, s);
       return true;
     default: return false;
   }
 }
 
+// The packed narrow last chunk of the light rows (ft_segsum_tail_kernel).
+template <int W>
+void launch_segsum_tail_w(const SegParams& p, cudaStream_t s) {
+  constexpr int G = 32 / W < 15 ? 32 / W : 15;  // rows per warp, as in ft_segsum_tail_kernel
+  const int64_t rows = p.row_end - p.row_begin;
+  count_launch();
+  ft_segsum_tail_kernel<W, 4><<<(unsigned)ceil_div(rows, 4 * G), 128, 0, s>>>(p);
+}
+
+// Launches the packed tail kernel for the last column chunk when it applies
+// (16-byte vectors addressed from dout[0], full-width chunks + a narrow tail);
+// returns whether it did.
+bool launch_segsum_tail(const SegParams& p, bool delta_ok, cudaStream_t s) {
+  if (!delta_ok || !p.g.exact || p.g.n_chunks < 2 || p.g.max_width > 32) return false;
+  switch (p.g.width(p.g.n_chunks - 1)) {
+    case 2: launch_segsum_tail_w<2>(p, s); return true;
+    case 3: launch_segsum_tail_w<3>(p, s); return true;
+    case 4: launch_segsum_tail_w<4>(p, s); return true;
+    case 6: launch_segsum_tail_w<6>(p, s); return true;
+    case 8: launch_segsum_tail_w<8>(p, s); return true;
+    default: return false;
+  }
+}
+
+// tail_done: the packed last chunk was already launched on the side stream.
 template <typename VT>
-void launch_segsum_light(const SegParams& p, bool queue_ok, cudaStream_t s) {
+void launch_segsum_light(const SegParams& p, bool queue_ok, bool delta_ok, bool tail_done, cudaStream_t s) {
   const int slot = timer_begin(kTimeLight, s);
-  if (!(std::is_same<VT, float4>::value && queue_ok && lanes_per_row(p.g) == 1 && launch_segsum_queue(p, s)))
-    launch_segsum_range<VT>(p, 0, p.g.n_chunks, p.g.max_width, s);
+  int n_chunks = p.g.n_chunks;
+  if (tail_done) --n_chunks;
+  else if (std::is_same<VT, float4>::value && g_tune.bwd_tail == 1 && launch_segsum_tail(p, delta_ok, s)) --n_chunks;
+  if (!(std::is_same<VT, float4>::value && queue_ok && lanes_per_row(p.g) == 1 && launch_segsum_queue(p, n_chunks, s)))
+    launch_segsum_range<VT>(p, 0, n_chunks, p.g.max_width, s);
   timer_end(slot, s);
 }
 
@@ -691,7 +775,7 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   // Queued light rows address both perspectives' gradient rows by 32-bit
   // offsets from dout[0]: usable when dout[1] - dout[0] (in vectors) plus any
   // row offset stays inside int32.
-  bool queue_ok = false;
+  bool queue_ok = false, delta_ok = false;
   if (v4) {
     const int64_t delta =
         ((int64_t)reinterpret_cast<uintptr_t>(p.dout[1]) - (int64_t)reinterpret_cast<uintptr_t>(p.dout[0])) / 16;
@@ -699,14 +783,15 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     // K / 4: the mean share of the K index slots that are active, measured on the
     // synthetic positions for both feature sets (41 of 160, 17 of 32)
     const int64_t expected_per_row = pl.B * pl.P * (int64_t)pl.K / (4 * std::max<int64_t>(pl.T, 1));
-    if (delta >= INT32_MIN && delta + span <= (int64_t)INT32_MAX + 1 &&
-        expected_per_row >= g_tune.bwd_queue_min_entries) {
+    if (delta >= INT32_MIN && delta + span <= (int64_t)INT32_MAX + 1) {
       p.persp_delta = (int32_t)delta;
-      queue_ok = true;
+      delta_ok = true;
+      queue_ok = expected_per_row >= g_tune.bwd_queue_min_entries;
     }
   }
 
   const bool rows = row_end > row_begin;
+  bool tail_done = false;
   DeviceAux* aux = nullptr;
   int rc = device_aux(&aux);
   if (rc != NNUE_OK) return rc;
@@ -715,6 +800,8 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     std::lock_guard<std::mutex> lock(g_aux_mu);
     if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
       return check_launch("backward_apply: fork");
+    // bwd_tail 2: the light rows' packed last chunk here, beside the main light-row kernel
+    if (rows && v4 && g_tune.bwd_tail == 2) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
     if (rows) {
       if (pl.P == 2 && pl.heavy_cap > 0 &&
           cudaMemsetAsync(w.hticket, 0, sizeof(uint32_t) * pl.heavy_cap * p.g.n_vec, aux->side) != cudaSuccess)
@@ -726,9 +813,9 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
   }
   if (rows && v4) {
-    launch_segsum_light<float4>(p, queue_ok, s);
+    launch_segsum_light<float4>(p, queue_ok, delta_ok, tail_done, s);
   } else if (rows) {
-    launch_segsum_light<float>(p, false, s);
+    launch_segsum_light<float>(p, false, false, false, s);
   }
   // A later record of `join` by another call is further down the same
   // in-order side stream, so waiting on it also covers this call's work.
@@ -958,17 +1045,19 @@ int nnue_ft_forward_pair_prepare(const int32_t* idx0, const int32_t* idx1, int64
   rc = device_aux(&aux);
   if (rc != NNUE_OK) return rc;
   {
-    // the backward's index-only phase runs on the side stream, concurrently
-    // with the forward gather on the caller's stream
+    // the backward's index-only phase (and the forward's packed tail chunk)
+    // run on the side stream, concurrently with the forward gather on the
+    // caller's stream
     std::lock_guard<std::mutex> lock(g_aux_mu);
     if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
       return check_launch("forward_pair_prepare: fork");
+    rc = forward_impl(idx0, idx1, 2, batch, max_active, weight, num_inputs, output_size, bias, out0, out1, s, nullptr,
+                      aux->side);
+    if (rc != NNUE_OK) return rc;
     rc = prepare_impl(idx0, idx1, pl, carve(pl, workspace), aux->side);
     if (rc != NNUE_OK) return rc;
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("forward_pair_prepare: join record");
   }
-  rc = forward_impl(idx0, idx1, 2, batch, max_active, weight, num_inputs, output_size, bias, out0, out1, s);
-  if (rc != NNUE_OK) return rc;
   if (cudaStreamWaitEvent(s, aux->join, 0) != cudaSuccess) return check_launch("forward_pair_prepare: join");
   return NNUE_OK;
 }

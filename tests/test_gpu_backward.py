@@ -281,3 +281,46 @@ def test_backward_rejects_max_active_beyond_counters(cuda):
     so max_active >= 65536 is refused instead of mis-sorted."""
     lib = _native.load()
     assert lib.nnue_ft_backward_workspace_size(4, 65536, 100, 8, 2) == 0
+
+
+@pytest.mark.parametrize("C,tail", [(1048, 6), (264, 2), (140, 3), (144, 4), (160, 8)])
+@pytest.mark.parametrize("case", ["plain", "heavy_in_warp", "long_light_rows", "accumulate"])
+def test_backward_packed_tail_chunk(cuda, C, tail, case):
+    """The light rows' narrow last column chunk packed 32 // tail rows per
+    warp (ft_segsum_tail_kernel): every width it is built for; a hot row
+    inside a packed warp and rows past the heavy-row cap (both take the
+    direct path); accumulate mode.  Bit-exact against the oracle and equal to
+    the unpacked chunk."""
+    assert (C // 4) % 32 == tail
+    T, B, K = 700, 2500, 12
+    i0 = random_indices(B, K, T, seed=C + 1)
+    i1 = random_indices(B, K, T, seed=C + 2)
+    params = {"bwd_queue_min_entries": 0}
+    if case in ("heavy_in_warp", "long_light_rows"):
+        i0[:, 0] = 17  # hot rows in the middle of a packed group
+        i1[::2, 3] = 18
+        i1[1::2, 3] = 503
+    if case == "long_light_rows":
+        params.update(heavy_threshold=4, heavy_cap=1)
+    g0, g1 = _grads(B, C, C + 3)
+    acc = case == "accumulate"
+    dW0 = random_table(T, C, seed=5, std=1.0) if acc else None
+    dB0 = random_table(1, C, seed=6, std=1.0)[0] if acc else None
+    got = {}
+    for packed in (2, 1, 0):  # side stream, caller's stream, not packed
+        p = dict(params, bwd_tail=packed)
+        got[packed] = _with_params(p, lambda: _bwd_pair(i0, i1, g0, g1, T, cuda, accumulate=acc,
+                                                        dW0=None if dW0 is None else dW0.copy(),
+                                                        dB0=None if dB0 is None else dB0.copy()))
+    if acc:
+        rW, rB = oracle.ft_backward(i0, g0, T, dW0.copy(), dB0.copy())
+        rW, rB = oracle.ft_backward(i1, g1, T, rW, rB)
+    else:
+        rW, rB = oracle.ft_backward_pair(i0, i1, g0, g1, T)
+    np.testing.assert_array_equal(got[1][0], got[0][0])
+    np.testing.assert_array_equal(got[2][0], got[0][0])
+    if not acc:
+        np.testing.assert_array_equal(got[1][0], rW)
+    else:
+        np.testing.assert_allclose(got[1][0], rW, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(got[1][1], rB, rtol=RTOL, atol=1e-5)

@@ -142,3 +142,42 @@ def test_forward_out_of_range_index_is_skipped_and_flagged(cuda):
     # a clean call raises nothing
     _fwd(idx, W, bias, cuda)
     assert _native.device_errors(clear=True) == 0
+
+
+@pytest.mark.parametrize("C,tail", [(1048, 6), (264, 2), (140, 3), (144, 4), (160, 8), (132, 1)])  # tail 1: not packed
+@pytest.mark.parametrize("K", [32, 160])
+def test_forward_packed_tail_chunk(cuda, C, tail, K):
+    """The narrow last column chunk packed 32 // tail items per warp
+    (ft_forward_tail_kernel): every width it is built for, one or five index
+    groups per item, a batch that does not fill the last packed group, both
+    the single and the pair forward; bit-exact against the oracle and equal
+    to the unpacked chunk."""
+    assert (C // 4) % 32 == tail
+    T, B = 3000, 1001
+    idx0 = random_indices(B, K, T, seed=C + K)
+    idx1 = random_indices(B, K, T, seed=C + K + 1)
+    W = random_table(T, C, seed=K, std=1.0)
+    bias = random_table(1, C, seed=C, std=1.0)[0]
+    dW, db = torch.from_numpy(W).to(cuda), torch.from_numpy(bias).to(cuda)
+    i0, i1 = torch.from_numpy(idx0).to(cuda), torch.from_numpy(idx1).to(cuda)
+    results = {}
+    for packed in (3, 2, 1, 0):  # large-batch auto, side stream, caller's stream, not packed
+        old = _native.get_param("fwd_tail")
+        _native.set_param("fwd_tail", packed)
+        try:
+            o0 = torch.empty(B, C, device=cuda)
+            o1 = torch.empty_like(o0)
+            ops.forward_pair_into(i0, i1, dW, db, o0, o1)
+            single = _fwd(idx0, W, bias, cuda)
+            p0, p1 = torch.empty_like(o0), torch.empty_like(o0)  # the prepare form forks a side stream
+            ops.forward_pair_prepare(i0, i1, dW, db, p0, p1, ops.alloc_workspace(B, K, T, C, 2, cuda))
+            torch.cuda.synchronize()
+        finally:
+            _native.set_param("fwd_tail", old)
+        results[packed] = (o0.cpu().numpy(), o1.cpu().numpy(), single, p0.cpu().numpy(), p1.cpu().numpy())
+    np.testing.assert_array_equal(results[1][0], oracle.ft_forward(idx0, W, bias))
+    np.testing.assert_array_equal(results[1][1], oracle.ft_forward(idx1, W, bias))
+    np.testing.assert_array_equal(results[1][2], results[1][0])
+    for packed in (3, 2, 1):
+        for a, b in zip(results[packed], results[0]):
+            np.testing.assert_array_equal(a, b)

@@ -94,8 +94,10 @@ int nnue_ft_device_errors(uint32_t *flags, int clear);
  * "fwd_min_blocks", "fwd_exact_chunks", "fwd_block", "fwd_groups",
  * "fwd_queue_blocks", "bwd_chunk_vec", "bwd_unroll", "bwd_min_blocks",
  * "bwd_exact_chunks", "bwd_block", "bwd_queue", "bwd_queue_min_blocks",
- * "bwd_queue_min_entries", "heavy_threshold", "heavy_cap",
- * "sort_blocks_per_sm", "colsum_parts"); unknown names and out-of-range
+ * "bwd_queue_min_entries", "fwd_tail", "bwd_tail",
+ * "heavy_threshold", "heavy_cap", "sort_blocks_per_sm", "colsum_parts");
+ * their meanings and defaults are beside struct Tuning in
+ * stockfish_trainer_b200/csrc/nnue_ft.cu.  Unknown names and out-of-range
  * values are rejected with
  * NNUE_ERR_INVALID_ARGUMENT.  Every setting gives the same results.
  * Process-wide; change them only while no call is in flight and never between

@@ -44,6 +44,21 @@ def test_version_and_params():
         _native.set_param("fwd_items_per_warp", 0)
 
 
+def _documented_knobs():
+    text = open(HEADER).read()
+    block = re.search(r"/\* Tuning knobs \(names: (.*?)\);", text, flags=re.S).group(1)
+    return re.findall(r'"(\w+)"', block)
+
+
+def test_every_documented_knob_is_readable():
+    knobs = _documented_knobs()
+    assert len(knobs) == len(set(knobs)) >= 20
+    for name in knobs:
+        v = _native.get_param(name)
+        _native.set_param(name, v)  # the default is inside its own range
+        assert _native.get_param(name) == v
+
+
 def test_host_side_argument_errors():
     lib = _native.load()
     # null pointers -> INVALID_ARGUMENT before any CUDA call

@@ -84,6 +84,11 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--serial-prepare", action="store_true",
                    help="run the backward's index phase after the forward instead of concurrently with it")
+    p.add_argument("--parallel", choices=["cols", "dp"], default="cols",
+                   help="N > 1: cols = each rank owns a column slice of the table and the ranks exchange "
+                        "outputs and output gradients (stockfish_trainer_b200.colsharded); dp = every rank "
+                        "holds the whole table and the weight gradient is allreduce-averaged (the reference's "
+                        "DDP scheme)")
     p.add_argument("--ddp-blocks", type=int, default=4,
                    help="N > 1: row blocks whose gradient allreduce overlaps the next block's backward "
                         "(0 = one allreduce after the whole backward)")
@@ -133,7 +138,7 @@ def timed_kernel_columns(C: int, tail_knob: int, items: int, forward: bool) -> i
     tail knob is on (forward mode 3: only from 2^17 items); that kernel is
     not timed with the main one."""
     n_vec, tail = C // 4, (C // 4) % 32
-    if C % 4 or n_vec < 64 or tail not in (2, 3, 4, 6, 8):
+    if C % 4 or n_vec < 32 or tail not in (2, 3, 4, 6, 8):
         return C
     mode = tail_knob
     if forward and mode == 3:
@@ -270,9 +275,14 @@ def cpu_baseline(white, black, T, seed, budget_s):
 
 
 def base_config(args, world, b_rank, T, K, nnz=None):
+    cols = world > 1 and getattr(args, "parallel", "dp") == "cols"
+    exchange = ""
+    if world > 1:
+        exchange = (", column-sharded table: index rows all-gathered, outputs and 1/N-scaled output gradients "
+                    "exchanged between ranks, each rank's columns of the averaged dW + dB") if cols else \
+            ", fp32 allreduce-mean"
     cfg = {
-        "workload": f"{args.feature_set} feature transformer fwd+bwd, both perspectives, dense dW + dB"
-                    + (", fp32 allreduce-mean" if world > 1 else ""),
+        "workload": f"{args.feature_set} feature transformer fwd+bwd, both perspectives, dense dW + dB" + exchange,
         "feature_set": args.feature_set,
         "global_batch": args.batch,
         "batch_per_gpu": b_rank,
@@ -280,7 +290,7 @@ def base_config(args, world, b_rank, T, K, nnz=None):
         "psqt": NPSQT,
         "num_inputs": T,
         "max_active": K,
-        "parallelism": f"dp{world}",
+        "parallelism": f"cols{world}" if cols else f"dp{world}",
         "l2": "inputs larger than L2 (126 MB), no flush",
     }
     if nnz is not None:
@@ -454,13 +464,53 @@ def run_ours(args):
     i1 = torch.from_numpy(black).to(dev)
     out0 = torch.empty(b_rank, C, device=dev)
     out1 = torch.empty_like(out0)
-    ws = ops.alloc_workspace(b_rank, K, T, C, 2, dev)
-    grads = ddp.GradientBuffer(T, C, dev)
+    cols = world > 1 and args.parallel == "cols"
+    if cols:
+        # this rank's kernels read its column slice of the table and run over
+        # every position of the global batch
+        from stockfish_trainer_b200 import colsharded
 
-    n_ev = 5
+        plan = colsharded.ColumnShardedFT(T, C, args.batch, K, device=dev)
+        Wk, bk, kc, kb = plan.shard_columns(W), plan.shard_columns(bias), plan.width, args.batch
+        W = None  # this rank keeps its columns only
+        ws = plan.workspace
+        plan.gather_indices(i0, i1)
+        ki0, ki1, ko0, ko1 = plan.idx[0], plan.idx[1], plan.y[0], plan.y[1]
+        knnz = nnz_all
+        kcounts = torch.bincount(plan.idx[plan.idx >= 0].long(), minlength=T).cpu().numpy()
+    else:
+        Wk, bk, kc, kb = W, bias, C, b_rank
+        ws = ops.alloc_workspace(b_rank, K, T, C, 2, dev)
+        ki0, ki1, ko0, ko1 = i0, i1, out0, out1
+        knnz = nnz_rank
+        kcounts = np.bincount(white[white >= 0], minlength=T) + np.bincount(black[black >= 0], minlength=T)
+    grads = ddp.GradientBuffer(T, kc, dev)
+
+    n_ev = 6 if cols else 5
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(max(args.steps, 1))]
 
+    def step_cols(e=None):
+        if e:
+            e[0].record()
+        plan.gather_indices(i0, i1)
+        if e:
+            e[1].record()
+        plan.forward_local(Wk, bk)
+        if e:
+            e[2].record()
+        plan.exchange_outputs(out0, out1)
+        if e:
+            e[3].record()
+        plan.exchange_grads(g0, g1)
+        if e:
+            e[4].record()
+        plan.backward_local(grads.weight, grads.bias)
+        if e:
+            e[5].record()
+
     def step(e=None):
+        if cols:
+            return step_cols(e)
         if e:
             e[0].record()
         if args.serial_prepare:
@@ -546,12 +596,10 @@ def run_ours(args):
     _native.kernel_timer_arm((), 0)
     ms_instrumented = max_over_ranks(start_i.elapsed_time(end_i)) / args.steps
     # with --ddp-blocks the "backward_apply" phase includes the overlapped allreduce
-    phases = {
-        ("forward" if args.serial_prepare else "forward+prepare"): [e[0].elapsed_time(e[1]) for e in ev[: args.steps]],
-        "backward_prepare": [e[1].elapsed_time(e[2]) for e in ev[: args.steps]],
-        "backward_apply": [e[2].elapsed_time(e[3]) for e in ev[: args.steps]],
-        "allreduce": [e[3].elapsed_time(e[4]) for e in ev[: args.steps]],
-    }
+    names = ["gather_indices", "forward+prepare", "exchange_outputs", "exchange_grads", "backward_apply"] if cols \
+        else ["forward" if args.serial_prepare else "forward+prepare", "backward_prepare", "backward_apply",
+              "allreduce"]
+    phases = {n: [e[i].elapsed_time(e[i + 1]) for e in ev[: args.steps]] for i, n in enumerate(names)}
     phase_ms = {k: max_over_ranks(float(np.mean(v))) for k, v in phases.items()}
     if _native.device_errors(clear=True):
         raise RuntimeError("device error flags raised during the instrumented steps")
@@ -574,17 +622,17 @@ def run_ours(args):
     # With the narrow last column chunk packed into its own kernel on the side
     # stream, the timed forward / light-row kernels cover the other columns
     # only: count the bytes of the columns each timed kernel covers.
-    c_fwd = timed_kernel_columns(C, _native.get_param("fwd_tail"), 2 * b_rank, forward=True)
-    c_light = timed_kernel_columns(C, _native.get_param("bwd_tail"), 2 * b_rank, forward=False)
-    counts = np.bincount(white[white >= 0], minlength=T) + np.bincount(black[black >= 0], minlength=T)
-    heavy = np.sort(counts[counts > _native.get_param("heavy_threshold")])[::-1][:_native.get_param("heavy_cap")]
+    # (column-sharded: the kernels cover every position on this rank's columns)
+    c_fwd = timed_kernel_columns(kc, _native.get_param("fwd_tail"), 2 * kb, forward=True)
+    c_light = timed_kernel_columns(kc, _native.get_param("bwd_tail"), 2 * kb, forward=False)
+    heavy = np.sort(kcounts[kcounts > _native.get_param("heavy_threshold")])[::-1][:_native.get_param("heavy_cap")]
     n_heavy, nnz_heavy = int(heavy.size), int(heavy.sum())
-    nnz_light = nnz_rank - nnz_heavy
-    a_fwd = nnz_rank * c_fwd * 4 + 2 * b_rank * c_fwd * 4 + 2 * b_rank * K * 4 + c_fwd * 4
+    nnz_light = knnz - nnz_heavy
+    a_fwd = knnz * c_fwd * 4 + 2 * kb * c_fwd * 4 + 2 * kb * K * 4 + c_fwd * 4
     a_light = nnz_light * (c_light * 4 + 4) + (2 * T + 1) * 4 + T + (T - n_heavy) * c_light * 4
-    a_heavy = nnz_heavy * (C * 4 + 4) + n_heavy * C * 4
-    a_step_survey = (nnz_rank * C * 4 + 2 * b_rank * C * 4 + 2 * b_rank * K * 4) + \
-                    (nnz_rank * C * 4 + 2 * b_rank * K * 4 + T * C * 4)
+    a_heavy = nnz_heavy * (kc * 4 + 4) + n_heavy * kc * 4
+    a_step_survey = (knnz * kc * 4 + 2 * kb * kc * 4 + 2 * kb * K * 4) + \
+                    (knnz * kc * 4 + 2 * kb * K * 4 + T * kc * 4)
     # DRAM bytes per launch from a one-pass ncu capture of this exact command
     # taken on the current kernel sources (other shapes: not captured)
     capture = captured_traffic()
@@ -614,7 +662,7 @@ def run_ours(args):
     barrier()
     for a, b in kev:
         a.record()
-        ops.forward_pair_into(i0, i1, W, bias, out0, out1)
+        ops.forward_pair_into(ki0, ki1, Wk, bk, ko0, ko1)
         b.record()
     barrier()
     fwd_alone_ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in kev])))
@@ -682,14 +730,18 @@ def run_ours(args):
     if not args.no_e2e:
         h0 = torch.from_numpy(white).pin_memory()
         h1 = torch.from_numpy(black).pin_memory()
-        host_out = torch.empty(C, dtype=torch.float32).pin_memory()
-        Wp = W.detach().clone().requires_grad_()
-        bp = bias.detach().clone().requires_grad_()
+        host_out = torch.empty(kc, dtype=torch.float32).pin_memory()
+        Wp = Wk.detach().clone().requires_grad_()
+        bp = bk.detach().clone().requires_grad_()
 
         def ft_pair(idx0, idx1):
             # one GPU: the reference-facing autograd function; N GPUs: its
-            # data-parallel form, whose backward returns the averaged gradients
-            # with the exchange overlapped in row blocks
+            # column-sharded form (this rank's columns as the parameters, its
+            # positions in and out) or its data-parallel form, whose backward
+            # returns the averaged gradients with the exchange overlapped in
+            # row blocks
+            if cols:
+                return colsharded.SparseLinearPairColumnSharded.apply(idx0, idx1, Wp, bp, plan)
             if world > 1:
                 return ddp.SparseLinearPairAllreduce.apply(idx0, idx1, Wp, bp, world, max(args.ddp_blocks, 1))
             return SparseLinearPairFunction.apply(idx0, idx1, Wp, bp)
@@ -855,11 +907,14 @@ def run_ours(args):
             positions.encode(sample, args.feature_set)
             host_enc = sample.shape[0] / (time.perf_counter() - t0)
         e2e = {"value": args.batch / (ms_e2e / 1e3), "unit": "positions/s",
-               "h2d_bytes_per_step": int(h0.numel() * 4 + h1.numel() * 4), "d2h_bytes_per_step": C * 4,
+               "h2d_bytes_per_step": int(h0.numel() * 4 + h1.numel() * 4), "d2h_bytes_per_step": kc * 4,
                "ms_per_step": ms_e2e,
-               "path": "SparseLinearPairFunction autograd fwd+bwd (N > 1: ddp.SparseLinearPairAllreduce, "
-                       "gradients averaged inside the backward); each step's indices copied from pinned "
-                       "host memory on a copy stream one step ahead (double-buffered); bias grad read back",
+               "path": "SparseLinearPairFunction autograd fwd+bwd (N > 1: "
+                       + ("colsharded.SparseLinearPairColumnSharded, this rank's columns of the averaged "
+                          "gradients" if cols else "ddp.SparseLinearPairAllreduce, gradients averaged inside "
+                                                   "the backward")
+                       + "); each step's indices copied from pinned host memory on a copy stream one step "
+                         "ahead (double-buffered); bias grad read back",
                "serial_copy_ms_per_step": ms_serial,
                "unchanged_caller": None if ms_unchanged is None else {
                    "value": args.batch / (ms_unchanged / 1e3), "unit": "positions/s", "ms_per_step": ms_unchanged,
@@ -869,7 +924,7 @@ def run_ours(args):
                            "autograd adding the two; same double-buffered host copies"},
                "boards": {"value": args.batch / (ms_boards / 1e3), "unit": "positions/s",
                           "ms_per_step": ms_boards, "h2d_bytes_per_step": int(hboard.numel()),
-                          "d2h_bytes_per_step": C * 4,
+                          "d2h_bytes_per_step": kc * 4,
                           "path": "boards [B, 64] uint8 copied from pinned host memory on a copy stream one "
                                   "step ahead (double-buffered), encoded on the device at the start of the "
                                   "step (nnue_ft_encode_features), then the same autograd step",

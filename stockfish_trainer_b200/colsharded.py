@@ -1,0 +1,330 @@
+"""Column-sharded feature transformer over the ranks of a process group.
+
+The reference trains data-parallel (src/train/common.py:186-199, 256-263,
+src/train/distributed.py:47-77): the global batch is split evenly over ranks,
+every rank holds the whole table and DDP averages the dense FT weight
+gradient -- T x C fp32, 357.6 MB at the headline size -- with an allreduce
+every step.  That exchange does not shrink as ranks are added, while each
+rank's share of the gathers does.
+
+Here rank r owns a slice of the table's COLUMNS (``column_slices``): its
+slice of the weight, of the bias and of any optimizer state, for all T rows.
+Every position's output row is bias + a sum of table rows, column by column,
+so a rank can produce its columns of every position's output, and the
+gradient of its columns needs only its columns of every position's output
+gradient.  One step:
+
+1. ``gather_indices``: every rank receives all ranks' index rows (int32,
+   B x K per perspective; they are inputs, known before the step);
+2. ``forward``: the pair forward + the backward's index phase over the WHOLE
+   batch on this rank's columns (the same kernels as one GPU), then an
+   exchange: rank r sends rows [s*b, (s+1)*b) of its columns to rank s, and
+   each rank joins the column blocks into its own positions' full rows
+   [b, C] -- what the data-parallel forward returns;
+3. ``backward``: the exchange the other way (rank r sends its positions'
+   output gradients of rank s's columns to s, scaled by 1/N: DDP's
+   averaging), then the segment sums over the whole batch on this rank's
+   columns -> this rank's columns of the averaged weight and bias gradients.
+
+Bytes over NVLink per rank and step, N ranks, global batch B, C columns,
+both perspectives: indices (N-1)/N * 2BK*4 in, outputs and output gradients
+(N-1)/N^2 * 2BC*4 each way, against an allreduce's 2(N-1)/N * TC*4 (ring).
+At the headline (B = 65536, K = 160, C = 1048, T = 85296): 42 + 137 + 137 MB
+at N = 2 against 358 MB; 73 + 60 + 60 MB at N = 8 against 626 MB.
+
+Sums are taken in the single-GPU order (ascending position per row, each
+perspective from zero, then added), so the gradient of rank r's columns is
+the one-GPU full-batch gradient of those columns times 1/N -- bit for bit
+when N is a power of two (the scale is exact), independent of the exchange.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+VECTOR = 4  # floats per 16-byte vector: slices are whole vectors when C % 4 == 0
+CHUNK = 32  # vectors per column chunk of the gather kernels (one per lane)
+PACKED_TAILS = (2, 3, 4, 6, 8)  # narrow last chunks that run in the packed tail kernels
+
+
+def _slice_cost(v: int) -> int:
+    """Relative gather cost of a v-vector column slice, in 1/1000 of a full
+    chunk: full 32-vector chunks cost one each; a narrow last chunk the
+    packed tail kernels take costs little; any other narrow chunk runs with
+    idle lanes in the main kernels at nearly a full chunk's instructions."""
+    full, tail = divmod(v, CHUNK)
+    if tail == 0:
+        return 1000 * full
+    if full and tail in PACKED_TAILS:
+        return 1000 * full + 100 + 10 * tail
+    return 1000 * full + 500 + (500 * tail) // CHUNK
+
+
+def column_slices(output_size: int, world: int) -> list[tuple[int, int]]:
+    """[(c0, c1)] per rank: contiguous column slices covering output_size.
+
+    With output_size a multiple of 4 every slice is whole 16-byte vectors
+    (the kernels' vector path), sized to minimise the slowest rank's gather
+    cost (``_slice_cost``), then the total, then the widest slice; otherwise
+    an even split of the columns.  Deterministic: every rank computes the
+    same list."""
+    if world < 1:
+        raise ValueError("world size must be >= 1")
+    if output_size < world:
+        raise ValueError(f"{output_size} columns cannot be split over {world} ranks")
+    if output_size % VECTOR:
+        return [(output_size * r // world, output_size * (r + 1) // world) for r in range(world)]
+    n = output_size // VECTOR
+    if n < world:
+        raise ValueError(f"{n} 16-byte column vectors cannot be split over {world} ranks")
+    lo_w, hi_w = max(1, n // world - 2 * CHUNK), n // world + 2 * CHUNK
+    # best[m] = (key, widths) over the ranks placed so far, m vectors used
+    best: dict[int, tuple[tuple[int, int, int], tuple[int, ...]]] = {0: ((0, 0, 0), ())}
+    for _ in range(world):
+        nxt: dict[int, tuple[tuple[int, int, int], tuple[int, ...]]] = {}
+        for m, ((mx, tot, wide), widths) in best.items():
+            for v in range(lo_w, hi_w + 1):
+                if m + v > n:
+                    break
+                c = _slice_cost(v)
+                cand = ((max(mx, c), tot + c, max(wide, v)), widths + (v,))
+                cur = nxt.get(m + v)
+                if cur is None or cand[0] < cur[0]:
+                    nxt[m + v] = cand
+        best = nxt
+    if n not in best:
+        raise ValueError(f"no column split of {n} vectors over {world} ranks")
+    widths = sorted(best[n][1], reverse=True)
+    out, c = [], 0
+    for v in widths:
+        out.append((c * VECTOR, (c + v) * VECTOR))
+        c += v
+    return out
+
+
+class _CudaKernels:
+    """The native kernels the column-sharded step calls (CPU tests substitute
+    reference implementations with the same signatures)."""
+
+    @staticmethod
+    def alloc_workspace(batch, max_active, num_inputs, width, device):
+        from .feature_transformer import ops
+
+        return ops.alloc_workspace(batch, max_active, num_inputs, width, 2, device)
+
+    @staticmethod
+    def forward_prepare(idx0, idx1, weight, bias, out0, out1, workspace):
+        from .feature_transformer import ops
+
+        ops.forward_pair_prepare(idx0, idx1, weight, bias, out0, out1, workspace)
+
+    @staticmethod
+    def backward_apply(grad0, grad1, batch, max_active, weight_grad, bias_grad, workspace):
+        from .feature_transformer import ops
+
+        ops.backward_apply(grad0, grad1, batch, max_active, weight_grad, bias_grad, False, workspace)
+
+
+class ColumnShardedFT:
+    """Buffers, column slices and collectives of the column-sharded FT step
+    for one process group (every rank constructs it with the same sizes).
+
+    ``batch`` is the GLOBAL batch (a multiple of the group size); each rank
+    passes its own ``batch / N`` positions' index rows and output gradients,
+    as in data-parallel training.  The rank's parameters are its column slice
+    ``weight[:, c0:c1]`` / ``bias[c0:c1]`` as contiguous tensors
+    (``shard_columns``).  One step in flight per object: ``forward`` fills the
+    workspace ``backward`` consumes."""
+
+    def __init__(self, num_inputs: int, output_size: int, batch: int, max_active: int, device=None, group=None,
+                 kernels=None):
+        self.group = group
+        dist_on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if dist_on else 1
+        self.rank = dist.get_rank(group) if dist_on else 0
+        if batch % self.world:
+            raise ValueError(f"global batch {batch} is not divisible by world size {self.world}")
+        self.T, self.C, self.B, self.K = int(num_inputs), int(output_size), int(batch), int(max_active)
+        self.b = self.B // self.world
+        self.slices = column_slices(self.C, self.world)
+        self.c0, self.c1 = self.slices[self.rank]
+        self.width = self.c1 - self.c0
+        self.widths = [c1 - c0 for c0, c1 in self.slices]
+        self.kernels = kernels or _CudaKernels()
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        dev = self.device
+        self.scale = 1.0 / self.world
+        # all positions' index rows, per perspective [B, K]
+        self.idx = torch.empty(2, self.B, self.K, dtype=torch.int32, device=dev)
+        # this rank's columns of every position's output / output gradient
+        self.y = torch.empty(2, self.B, self.width, device=dev)
+        self.d = torch.empty(2, self.B, self.width, device=dev)
+        # per peer s: its columns of this rank's positions (received outputs,
+        # sent gradients), [2, b, w_s] blocks packed peer by peer
+        self.blk_off = [0]
+        for w in self.widths:
+            self.blk_off.append(self.blk_off[-1] + 2 * self.b * w)
+        self.recv = torch.empty(self.blk_off[-1], device=dev)
+        self.send = torch.empty(self.blk_off[-1], device=dev)
+        self.workspace = self.kernels.alloc_workspace(self.B, self.K, self.T, self.width, dev)
+
+    # -- parameters ---------------------------------------------------------
+    def shard_columns(self, full: torch.Tensor) -> torch.Tensor:
+        """This rank's columns of a [T, C] table or [C] vector, contiguous."""
+        return full[..., self.c0:self.c1].contiguous()
+
+    def gather_columns(self, cols: torch.Tensor) -> torch.Tensor:
+        """The whole [T, C] table (or [C] vector) from every rank's columns
+        (for checkpoints and export; a collective)."""
+        if self.world == 1:
+            return cols.clone()
+        parts = []
+        for s, w in enumerate(self.widths):
+            shape = list(cols.shape)
+            shape[-1] = w
+            parts.append(cols.contiguous() if s == self.rank else torch.empty(shape, dtype=cols.dtype,
+                                                                               device=cols.device))
+        for s in range(self.world):
+            dist.broadcast(parts[s], src=self._global(s), group=self.group)
+        return torch.cat(parts, dim=-1)
+
+    # -- collectives ----------------------------------------------------------
+    def _global(self, s: int) -> int:
+        return dist.get_global_rank(self.group, s) if self.group is not None else s
+
+    def _block(self, buf: torch.Tensor, s: int, p: int) -> torch.Tensor:
+        w = self.widths[s]
+        o = self.blk_off[s] + p * self.b * w
+        return buf[o:o + self.b * w].view(self.b, w)
+
+    def _exchange(self, sends, recvs) -> None:
+        """Point-to-point exchange: sends = [(peer, tensor)], recvs = [(peer,
+        tensor)], in the same per-peer order on every rank (one NCCL group)."""
+        ops = [dist.P2POp(dist.isend, t, self._global(s), self.group) for s, t in sends]
+        ops += [dist.P2POp(dist.irecv, t, self._global(s), self.group) for s, t in recvs]
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+
+    def gather_indices(self, idx0: torch.Tensor, idx1: torch.Tensor):
+        """Every rank's [b, K] index rows -> all positions' rows [B, K] per
+        perspective (rank s's rows at [s*b, (s+1)*b))."""
+        for p, x in enumerate((idx0, idx1)):
+            if tuple(x.shape) != (self.b, self.K):
+                raise ValueError(f"index rows must be [{self.b}, {self.K}], got {tuple(x.shape)}")
+            if self.world == 1:
+                self.idx[p].copy_(x)
+            elif dist.get_backend(self.group) == "nccl":
+                dist.all_gather_into_tensor(self.idx[p], x.contiguous(), group=self.group)
+            else:
+                parts = list(self.idx[p].view(self.world, self.b, self.K).unbind(0))
+                tmp = [torch.empty_like(t) for t in parts]
+                dist.all_gather(tmp, x.contiguous(), group=self.group)
+                for t, u in zip(parts, tmp):
+                    t.copy_(u)
+        return self.idx[0], self.idx[1]
+
+    # -- the step -------------------------------------------------------------
+    def forward_local(self, weight_cols: torch.Tensor, bias_cols: torch.Tensor) -> None:
+        """The pair forward + the backward's index phase over all positions
+        (``gather_indices`` first) on this rank's columns."""
+        if tuple(weight_cols.shape) != (self.T, self.width) or tuple(bias_cols.shape) != (self.width,):
+            raise ValueError(f"this rank's parameters must be [{self.T}, {self.width}] and [{self.width}]")
+        self.kernels.forward_prepare(self.idx[0], self.idx[1], weight_cols, bias_cols, self.y[0], self.y[1],
+                                     self.workspace)
+
+    def exchange_outputs(self, out0: Optional[torch.Tensor] = None, out1: Optional[torch.Tensor] = None):
+        """Rank s receives rows [s*b, (s+1)*b) of every rank's columns; each
+        rank joins them into its positions' full output rows [b, C]."""
+        r, b = self.rank, self.b
+        sends, recvs = [], []
+        for s in range(self.world):
+            if s == r:
+                continue
+            for p in range(2):
+                sends.append((s, self.y[p, s * b:(s + 1) * b]))
+                recvs.append((s, self._block(self.recv, s, p)))
+        self._exchange(sends, recvs)
+        outs = []
+        for p, o in enumerate((out0, out1)):
+            parts = [self.y[p, r * b:(r + 1) * b] if s == r else self._block(self.recv, s, p)
+                     for s in range(self.world)]
+            if o is None:
+                o = torch.empty(b, self.C, device=self.y.device)
+            torch.cat(parts, dim=1, out=o)
+            outs.append(o)
+        return outs[0], outs[1]
+
+    def exchange_grads(self, grad0: torch.Tensor, grad1: torch.Tensor) -> None:
+        """This rank's positions' output gradients [b, C] -> every rank
+        receives its columns of them (scaled by 1/N), rows in position order."""
+        r, b = self.rank, self.b
+        for p, g in enumerate((grad0, grad1)):
+            if tuple(g.shape) != (b, self.C):
+                raise ValueError(f"output gradients must be [{b}, {self.C}], got {tuple(g.shape)}")
+            for s, (c0, c1) in enumerate(self.slices):
+                dst = self.d[p, r * b:(r + 1) * b] if s == r else self._block(self.send, s, p)
+                torch.mul(g[:, c0:c1], self.scale, out=dst)
+        sends, recvs = [], []
+        for s in range(self.world):
+            if s == r:
+                continue
+            for p in range(2):
+                sends.append((s, self._block(self.send, s, p)))
+                recvs.append((s, self.d[p, s * b:(s + 1) * b]))
+        self._exchange(sends, recvs)
+
+    def backward_local(self, weight_grad_cols: torch.Tensor, bias_grad_cols: torch.Tensor) -> None:
+        """The segment sums over all positions on this rank's columns (after
+        ``exchange_grads``; needs the workspace of ``forward_local``)."""
+        self.kernels.backward_apply(self.d[0], self.d[1], self.B, self.K, weight_grad_cols, bias_grad_cols,
+                                    self.workspace)
+
+    def forward(self, weight_cols: torch.Tensor, bias_cols: torch.Tensor, idx0: torch.Tensor, idx1: torch.Tensor,
+                out0: Optional[torch.Tensor] = None, out1: Optional[torch.Tensor] = None):
+        """This rank's positions' outputs [b, C] per perspective (the
+        data-parallel forward's result) from its positions' index rows; also
+        runs the backward's index phase over the whole batch."""
+        self.gather_indices(idx0, idx1)
+        self.forward_local(weight_cols, bias_cols)
+        return self.exchange_outputs(out0, out1)
+
+    def backward(self, grad0: torch.Tensor, grad1: torch.Tensor, weight_grad_cols: torch.Tensor,
+                 bias_grad_cols: torch.Tensor) -> None:
+        """From this rank's positions' output gradients [b, C]: this rank's
+        columns of the weight and bias gradients averaged over the group
+        (written, not accumulated).  Needs the workspace of ``forward``."""
+        self.exchange_grads(grad0, grad1)
+        self.backward_local(weight_grad_cols, bias_grad_cols)
+
+
+class SparseLinearPairColumnSharded(torch.autograd.Function):
+    """``SparseLinearPairFunction`` for column-sharded training:
+    (idx_white, idx_black, weight_cols, bias_cols, sharded) -> (out_white,
+    out_black), the inputs and outputs this rank's ``batch / N`` positions,
+    the parameters this rank's column slice; the backward returns the
+    group-averaged gradients of that slice (what DDP's allreduce gives the
+    data-parallel form, restricted to the rank's columns).  Leave the two
+    parameters out of any other gradient averaging."""
+
+    @staticmethod
+    def forward(ctx, feature_indices_0, feature_indices_1, weight_cols, bias_cols, sharded: ColumnShardedFT):
+        out0, out1 = sharded.forward(weight_cols, bias_cols, feature_indices_0, feature_indices_1)
+        ctx.sharded = sharded
+        ctx.shapes = (tuple(weight_cols.shape), weight_cols.device)
+        return out0, out1
+
+    @staticmethod
+    def backward(ctx, grad0, grad1):
+        sh = ctx.sharded
+        (T, w), dev = ctx.shapes
+        # a missing output gradient counts as zeros, so every rank runs the same exchanges
+        g0 = grad0.contiguous() if grad0 is not None else torch.zeros(sh.b, sh.C, device=dev)
+        g1 = grad1.contiguous() if grad1 is not None else torch.zeros(sh.b, sh.C, device=dev)
+        dW = torch.empty(T, w, device=dev)
+        dB = torch.empty(w, device=dev)
+        sh.backward(g0, g1, dW, dB)
+        return None, None, dW, dB, None

@@ -84,7 +84,7 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--serial-prepare", action="store_true",
                    help="run the backward's index phase after the forward instead of concurrently with it")
-    p.add_argument("--parallel", choices=["cols", "dp"], default="cols",
+    p.add_argument("--parallel", choices=["cols", "dp"], default="dp",
                    help="N > 1: cols = each rank owns a column slice of the table and the ranks exchange "
                         "outputs and output gradients (stockfish_trainer_b200.colsharded); dp = every rank "
                         "holds the whole table and the weight gradient is allreduce-averaged (the reference's "

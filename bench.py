@@ -89,6 +89,9 @@ def parse_args():
                         "outputs and output gradients (stockfish_trainer_b200.colsharded); dp = every rank "
                         "holds the whole table and the weight gradient is allreduce-averaged (the reference's "
                         "DDP scheme)")
+    p.add_argument("--exchange", choices=["peer", "p2p"], default=None,
+                   help="--parallel cols: peer = this library's exchange kernel storing into the other GPUs' "
+                        "buffers (the default), p2p = torch.distributed point-to-point operations")
     p.add_argument("--ddp-blocks", type=int, default=4,
                    help="N > 1: row blocks whose gradient allreduce overlaps the next block's backward "
                         "(0 = one allreduce after the whole backward)")
@@ -470,10 +473,11 @@ def run_ours(args):
         # every position of the global batch
         from stockfish_trainer_b200 import colsharded
 
-        plan = colsharded.ColumnShardedFT(T, C, args.batch, K, device=dev)
+        plan = colsharded.ColumnShardedFT(T, C, args.batch, K, device=dev, exchange=args.exchange)
         Wk, bk, kc, kb = plan.shard_columns(W), plan.shard_columns(bias), plan.width, args.batch
         W = None  # this rank keeps its columns only
         ws = plan.workspace
+        dist.barrier()  # every rank arrives at its first exchange together
         plan.gather_indices(i0, i1)
         ki0, ki1, ko0, ko1 = plan.idx[0], plan.idx[1], plan.y[0], plan.y[1]
         knnz = nnz_all
@@ -498,7 +502,7 @@ def run_ours(args):
         plan.forward_local(Wk, bk)
         if e:
             e[2].record()
-        plan.exchange_outputs(out0, out1)
+        plan.exchange_outputs()
         if e:
             e[3].record()
         plan.exchange_grads(g0, g1)
@@ -961,7 +965,8 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "f32",
             "data": DATA,
-            "config": base_config(args, world, b_rank, T, K, int(nnz_all)),
+            "config": dict(base_config(args, world, b_rank, T, K, int(nnz_all)),
+                           **({"exchange": plan.exchange, "column_slices": plan.slices} if cols else {})),
             "phases_ms": phase_ms,
             "instrumented_ms_per_step": ms_instrumented,
             "roofline": roofline,
@@ -974,6 +979,8 @@ def run_ours(args):
             "gpu": torch.cuda.get_device_name(dev),
         }
         emit(line)
+    if cols:
+        plan.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

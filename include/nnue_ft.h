@@ -59,6 +59,7 @@ extern "C" {
 #define NNUE_DEVERR_BAD_SEGMENT 4u       /* backward: corrupt workspace (position out of range) */
 #define NNUE_DEVERR_BAD_PSQT_INDEX 8u    /* epilogue: PSQT bucket index outside [0, n_psqt) was skipped */
 #define NNUE_DEVERR_BAD_POSITION 16u     /* device encoder: a rejected position got all -1 rows */
+#define NNUE_DEVERR_EXCHANGE_TIMEOUT 32u /* exchange: a rank did not reach the barrier in time */
 
 /* ABI version (major * 100 + minor). */
 int nnue_ft_version(void);
@@ -356,6 +357,56 @@ int nnue_encode_features(const uint8_t *board, int64_t count, int32_t feature_se
  * (13 KB, into a static device array) synchronously. */
 int nnue_ft_encode_features(const uint8_t *board, int64_t count, int32_t feature_set, int32_t *white,
                             int32_t *black, int32_t *white_count, int32_t *black_count, void *stream);
+
+/* ---- exchange between the GPUs of one node --------------------------------
+ * The multi-GPU plumbing of the column-sharded FT step (no reference
+ * counterpart: the reference's DDP allreduces the dense weight gradient,
+ * src/train/common.py:186-199; this moves index rows, outputs and output
+ * gradients instead).  Each rank allocates one exchange buffer
+ * (nnue_ft_exchange_alloc, an exception to "nothing here allocates": a
+ * buffer of its own, so its IPC handle maps exactly it), shares the handle
+ * with the other ranks of the node (any host channel) and maps theirs
+ * (nnue_ft_exchange_open).  The buffer's first 64 bytes are the rank's flag
+ * words (zeroed at allocation); the rest is the caller's. */
+#define NNUE_FT_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc'd + zeroed buffer of `bytes` and its CUDA IPC handle
+ * (NNUE_FT_IPC_HANDLE_BYTES bytes).  Synchronous.  Free with
+ * nnue_ft_exchange_free. */
+int nnue_ft_exchange_alloc(size_t bytes, void **ptr, void *ipc_handle);
+int nnue_ft_exchange_free(void *ptr);
+
+/* Maps another process's exchange buffer into this process for the current
+ * device (peer access enabled as needed); nnue_ft_exchange_close unmaps. */
+int nnue_ft_exchange_open(const void *ipc_handle, void **ptr);
+int nnue_ft_exchange_close(void *ptr);
+
+/* One block copy: `rows` rows of `width` 16-byte vectors from src (row stride
+ * src_ld vectors) to dst (row stride dst_ld vectors); every float is
+ * multiplied by `scale` unless scale == 1 (then the bytes are copied as
+ * they are).  src is this GPU's memory; dst this GPU's or a mapped peer's.
+ * Both 16-byte aligned. */
+typedef struct {
+  const void *src;
+  void *dst;
+  int64_t rows;
+  int64_t src_ld, dst_ld;
+  int32_t width;
+  float scale;
+} nnue_ft_copy_desc;
+
+/* Runs up to 32 copies in one launch, then a barrier of the n_ranks (<= 15)
+ * ranks: flags[s] = rank s's flag words (its exchange buffer's start, mapped
+ * here; flags[rank] = this rank's own).  Every rank calls it in the same
+ * order with the same epoch, which must grow by one per call (the first
+ * call after allocation uses 1).  When the launch completes on this
+ * rank's stream, every rank's copies of this epoch are done and visible.
+ * A rank that does not arrive within timeout_ms raises
+ * NNUE_DEVERR_EXCHANGE_TIMEOUT and the launch returns without it (the
+ * exchanged data is then incomplete).  Not capturable in a CUDA graph
+ * (the epoch is a launch argument).  n_copies == 0: the barrier alone. */
+int nnue_ft_exchange(const nnue_ft_copy_desc *copies, int32_t n_copies, uint32_t *const *flags, int32_t n_ranks,
+                     int32_t rank, uint32_t epoch, int32_t timeout_ms, void *stream);
 
 #ifdef __cplusplus
 }

@@ -29,6 +29,7 @@ DEVERR_BAD_INDEX = 1
 DEVERR_BAD_QUANT_INDEX = 2
 DEVERR_BAD_PSQT_INDEX = 8
 DEVERR_BAD_POSITION = 16
+DEVERR_EXCHANGE_TIMEOUT = 32
 
 _SIGNATURES = {
     "nnue_ft_version": (_I32, []),
@@ -67,6 +68,11 @@ _SIGNATURES = {
     "nnue_generate_positions": (_I32, [_U64, _I64, _I64, _P, _P]),
     "nnue_encode_features": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _I32]),
     "nnue_ft_encode_features": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _P]),
+    "nnue_ft_exchange_alloc": (_I32, [_SZ, ctypes.POINTER(_P), _P]),
+    "nnue_ft_exchange_free": (_I32, [_P]),
+    "nnue_ft_exchange_open": (_I32, [_P, ctypes.POINTER(_P)]),
+    "nnue_ft_exchange_close": (_I32, [_P]),
+    "nnue_ft_exchange": (_I32, [_P, _I32, _P, _I32, _I32, ctypes.c_uint32, _I32, _P]),
 }
 
 _lib = None

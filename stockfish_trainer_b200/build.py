@@ -25,7 +25,7 @@ LIB_PATH = os.path.join(PKG, LIB_NAME)
 
 SOURCES = ["nnue_ft.cu", "features.cpp"]
 DEPS = SOURCES + ["common.cuh", "ft_forward.cuh", "ft_backward.cuh", "ft_quant.cuh", "ft_epilogue.cuh",
-                  "ft_optim.cuh", "ft_encode.cuh", "feature_tables.h", "feature_encode.h"]
+                  "ft_optim.cuh", "ft_encode.cuh", "ft_exchange.cuh", "feature_tables.h", "feature_encode.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

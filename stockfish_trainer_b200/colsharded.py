@@ -45,6 +45,32 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+class _CudaArray:
+    """A raw device allocation as a tensor (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _device_view(ptr: int, shape, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    typestr = {torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device=device)
+
+
+def _copy_desc_type():
+    import ctypes
+
+    class CopyDesc(ctypes.Structure):  # nnue_ft_copy_desc
+        _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("rows", ctypes.c_int64),
+                    ("src_ld", ctypes.c_int64), ("dst_ld", ctypes.c_int64), ("width", ctypes.c_int32),
+                    ("scale", ctypes.c_float)]
+
+    return CopyDesc
+
+
+_CopyDesc = _copy_desc_type()
+
 VECTOR = 4  # floats per 16-byte vector: slices are whole vectors when C % 4 == 0
 CHUNK = 32  # vectors per column chunk of the gather kernels (one per lane)
 PACKED_TAILS = (2, 3, 4, 6, 8)  # narrow last chunks that run in the packed tail kernels
@@ -137,11 +163,26 @@ class ColumnShardedFT:
     as in data-parallel training.  The rank's parameters are its column slice
     ``weight[:, c0:c1]`` / ``bias[c0:c1]`` as contiguous tensors
     (``shard_columns``).  One step in flight per object: ``forward`` fills the
-    workspace ``backward`` consumes."""
+    workspace ``backward`` consumes.
+
+    ``exchange``: "peer" (the default on CUDA tensors in an NCCL group of at
+    most 15 ranks with C and K multiples of 4) moves the data with this
+    library's exchange kernel, which stores straight into the other GPUs'
+    buffers (CUDA IPC) in the layout the receiver uses -- index rows at their
+    global positions, output blocks at their column offsets, 1/N-scaled
+    gradient blocks at their row offsets -- and ends with a bounded barrier
+    (a rank that does not arrive within ``timeout_ms`` raises
+    NNUE_DEVERR_EXCHANGE_TIMEOUT instead of hanging); "p2p" uses
+    ``torch.distributed`` point-to-point operations (any backend) and joins
+    the blocks with torch ops.  With "peer" the returned outputs live in the
+    exchange buffer, two steps' worth: a step's outputs stay valid until the
+    forward after the next one.  Call ``close`` on every rank (it is a
+    collective) before the process group goes away."""
 
     def __init__(self, num_inputs: int, output_size: int, batch: int, max_active: int, device=None, group=None,
-                 kernels=None):
+                 kernels=None, exchange: Optional[str] = None, timeout_ms: int = 5000):
         self.group = group
+        self.timeout_ms = int(timeout_ms)
         dist_on = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if dist_on else 1
         self.rank = dist.get_rank(group) if dist_on else 0
@@ -157,19 +198,114 @@ class ColumnShardedFT:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         dev = self.device
         self.scale = 1.0 / self.world
-        # all positions' index rows, per perspective [B, K]
-        self.idx = torch.empty(2, self.B, self.K, dtype=torch.int32, device=dev)
-        # this rank's columns of every position's output / output gradient
+        # this rank's columns of every position's output
         self.y = torch.empty(2, self.B, self.width, device=dev)
-        self.d = torch.empty(2, self.B, self.width, device=dev)
-        # per peer s: its columns of this rank's positions (received outputs,
-        # sent gradients), [2, b, w_s] blocks packed peer by peer
-        self.blk_off = [0]
-        for w in self.widths:
-            self.blk_off.append(self.blk_off[-1] + 2 * self.b * w)
-        self.recv = torch.empty(self.blk_off[-1], device=dev)
-        self.send = torch.empty(self.blk_off[-1], device=dev)
         self.workspace = self.kernels.alloc_workspace(self.B, self.K, self.T, self.width, dev)
+        self._peer = None
+        self._slot = 0
+        if exchange is None:
+            exchange = "peer" if self._peer_capable() else "p2p"
+        if exchange == "peer":
+            self._setup_peer_exchange()
+        elif exchange != "p2p":
+            raise ValueError(f"exchange must be 'peer' or 'p2p', got {exchange!r}")
+        self.exchange = exchange
+        if exchange == "p2p":
+            # all positions' index rows, per perspective [B, K]
+            self.idx = torch.empty(2, self.B, self.K, dtype=torch.int32, device=dev)
+            # this rank's columns of every position's output gradient
+            self.d = torch.empty(2, self.B, self.width, device=dev)
+            # per peer s: its columns of this rank's positions (received
+            # outputs, sent gradients), [2, b, w_s] blocks packed peer by peer
+            self.blk_off = [0]
+            for w in self.widths:
+                self.blk_off.append(self.blk_off[-1] + 2 * self.b * w)
+            self.recv = torch.empty(self.blk_off[-1], device=dev)
+            self.send = torch.empty(self.blk_off[-1], device=dev)
+
+    # -- peer exchange setup ---------------------------------------------------
+    _FLAG_BYTES = 256
+
+    def _peer_capable(self) -> bool:
+        if self.device.type != "cuda" or self.world > 15 or self.C % VECTOR or self.K % VECTOR:
+            return False
+        if self.world == 1:
+            return True
+        return dist.get_backend(self.group) == "nccl"
+
+    def _setup_peer_exchange(self) -> None:
+        import ctypes
+
+        from . import _native
+
+        def up(n):  # 256-byte aligned offsets
+            return (n + 255) // 256 * 256
+
+        f32 = 4
+        off_idx = self._FLAG_BYTES
+        off_out = off_idx + up(2 * self.B * self.K * 4)
+        off_d = off_out + up(2 * 2 * self.b * self.C * f32)  # two steps' outputs
+        total = off_d + up(2 * self.B * max(self.widths) * f32)
+        with torch.cuda.device(self.device):
+            base = ctypes.c_void_p(0)
+            handle = ctypes.create_string_buffer(64)
+            _native.call("nnue_ft_exchange_alloc", total, ctypes.byref(base), handle)
+            handles = [None] * self.world
+            if self.world > 1:
+                dist.all_gather_object(handles, handle.raw, group=self.group)
+            else:
+                handles[0] = handle.raw
+            bases = []
+            for s, h in enumerate(handles):
+                if s == self.rank:
+                    bases.append(base.value)
+                    continue
+                p = ctypes.c_void_p(0)
+                _native.call("nnue_ft_exchange_open", ctypes.create_string_buffer(h, 64), ctypes.byref(p))
+                bases.append(p.value)
+        self._peer = {"base": bases, "own": base.value, "off_idx": off_idx, "off_out": off_out, "off_d": off_d,
+                      "epoch": 0, "flags": (ctypes.c_void_p * self.world)(*bases), "total": total}
+        own = base.value
+        self.idx = _device_view(own + off_idx, (2, self.B, self.K), torch.int32, self.device)
+        self._out = [_device_view(own + off_out + i * 2 * self.b * self.C * f32, (2, self.b, self.C), torch.float32,
+                                  self.device) for i in range(2)]
+        self.d = _device_view(own + off_d, (2, self.B, self.width), torch.float32, self.device)
+
+    def close(self) -> None:
+        """Unmap the other ranks' exchange buffers and free this rank's (a
+        collective: every rank calls it once its exchanges are done)."""
+        if self._peer is None:
+            return
+        from . import _native
+
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # nobody writes into a buffer after this
+        with torch.cuda.device(self.device):
+            for s, b in enumerate(self._peer["base"]):
+                if s != self.rank:
+                    _native.call("nnue_ft_exchange_close", b)
+            if self.world > 1:
+                dist.barrier(group=self.group)  # every mapping of this rank's buffer is gone
+            _native.call("nnue_ft_exchange_free", self._peer["own"])
+        self._peer = None
+        self.idx = self.d = self._out = None
+
+    def _peer_exchange(self, copies) -> None:
+        """copies: [(src_ptr, dst_ptr, rows, src_ld, dst_ld, width, scale)],
+        strides and widths in 16-byte vectors."""
+        import ctypes
+
+        from . import _native
+
+        arr = (_CopyDesc * max(len(copies), 1))()
+        for i, (src, dst, rows, sld, dld, w, sc) in enumerate(copies):
+            arr[i] = _CopyDesc(src, dst, rows, sld, dld, w, sc)
+        self._peer["epoch"] += 1
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _native.call("nnue_ft_exchange", arr, len(copies), self._peer["flags"], self.world, self.rank,
+                         self._peer["epoch"] & 0xFFFFFFFF, self.timeout_ms, stream)
 
     # -- parameters ---------------------------------------------------------
     def shard_columns(self, full: torch.Tensor) -> torch.Tensor:
@@ -212,9 +348,20 @@ class ColumnShardedFT:
     def gather_indices(self, idx0: torch.Tensor, idx1: torch.Tensor):
         """Every rank's [b, K] index rows -> all positions' rows [B, K] per
         perspective (rank s's rows at [s*b, (s+1)*b))."""
-        for p, x in enumerate((idx0, idx1)):
+        for x in (idx0, idx1):
             if tuple(x.shape) != (self.b, self.K):
                 raise ValueError(f"index rows must be [{self.b}, {self.K}], got {tuple(x.shape)}")
+        if self._peer is not None:
+            xs = [x.contiguous() for x in (idx0, idx1)]
+            kv = self.K // VECTOR
+            copies = []
+            for s in range(self.world):
+                for p in range(2):
+                    dst = self._peer["base"][s] + self._peer["off_idx"] + (p * self.B + self.rank * self.b) * self.K * 4
+                    copies.append((xs[p].data_ptr(), dst, self.b, kv, kv, kv, 1.0))
+            self._peer_exchange(copies)
+            return self.idx[0], self.idx[1]
+        for p, x in enumerate((idx0, idx1)):
             if self.world == 1:
                 self.idx[p].copy_(x)
             elif dist.get_backend(self.group) == "nccl":
@@ -240,6 +387,23 @@ class ColumnShardedFT:
         """Rank s receives rows [s*b, (s+1)*b) of every rank's columns; each
         rank joins them into its positions' full output rows [b, C]."""
         r, b = self.rank, self.b
+        if self._peer is not None:
+            self._slot ^= 1
+            wv, cv = self.width // VECTOR, self.C // VECTOR
+            copies = []
+            for s in range(self.world):
+                for p in range(2):
+                    src = self.y[p, s * b].data_ptr()
+                    dst = self._peer["base"][s] + self._peer["off_out"] + \
+                        ((self._slot * 2 + p) * b * self.C + self.c0) * 4
+                    copies.append((src, dst, b, wv, cv, wv, 1.0))
+            self._peer_exchange(copies)
+            res = self._out[self._slot]
+            if out0 is not None:
+                out0.copy_(res[0])
+            if out1 is not None:
+                out1.copy_(res[1])
+            return (res[0] if out0 is None else out0), (res[1] if out1 is None else out1)
         sends, recvs = [], []
         for s in range(self.world):
             if s == r:
@@ -262,9 +426,22 @@ class ColumnShardedFT:
         """This rank's positions' output gradients [b, C] -> every rank
         receives its columns of them (scaled by 1/N), rows in position order."""
         r, b = self.rank, self.b
-        for p, g in enumerate((grad0, grad1)):
+        for g in (grad0, grad1):
             if tuple(g.shape) != (b, self.C):
                 raise ValueError(f"output gradients must be [{b}, {self.C}], got {tuple(g.shape)}")
+        if self._peer is not None:
+            gs = [g.contiguous() for g in (grad0, grad1)]
+            cv = self.C // VECTOR
+            copies = []
+            for s, (c0, c1) in enumerate(self.slices):
+                ws = c1 - c0
+                for p in range(2):
+                    src = gs[p].data_ptr() + c0 * 4
+                    dst = self._peer["base"][s] + self._peer["off_d"] + (p * self.B + r * b) * ws * 4
+                    copies.append((src, dst, b, cv, ws // VECTOR, ws // VECTOR, self.scale))
+            self._peer_exchange(copies)
+            return
+        for p, g in enumerate((grad0, grad1)):
             for s, (c0, c1) in enumerate(self.slices):
                 dst = self.d[p, r * b:(r + 1) * b] if s == r else self._block(self.send, s, p)
                 torch.mul(g[:, c0:c1], self.scale, out=dst)

@@ -22,6 +22,7 @@ enum : unsigned {
   kErrBadSegment = 4u,     // backward: a sorted position outside [0, batch) (corrupt workspace)
   kErrBadPsqtIndex = 8u,   // epilogue: PSQT bucket index outside [0, n_psqt)
   kErrBadPosition = 16u,   // encoder: a position the feature functions reject (its rows are all -1)
+  kErrExchangeTimeout = 32u,  // exchange: a rank did not arrive at the barrier in time
 };
 
 __device__ __forceinline__ void flag_error(unsigned e) { atomicOr(&g_device_errors, e); }

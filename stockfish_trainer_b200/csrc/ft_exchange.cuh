@@ -1,0 +1,114 @@
+// Exchange between the GPUs of one node for the column-sharded FT step:
+// block copies into this GPU's and other GPUs' memory (CUDA IPC mappings,
+// written with plain stores over NVLink / NVSwitch), followed by a barrier
+// among the ranks of the group through flag words in each rank's exchange
+// buffer.
+//
+// Every rank launches the same sequence of exchanges with the same epoch.
+// One launch: all blocks copy their rows; each block then makes its stores
+// visible system-wide (fence.sc.sys) and counts itself done; the last block
+// writes `epoch` into flag[rank] of every rank (st.release.sys) and waits
+// until its own flag[0 .. n_ranks) all reach `epoch` (ld.acquire.sys).  Only
+// then does the launch complete, so work after it in the stream sees every
+// rank's copies into this GPU's memory.  The wait is bounded in time: past
+// the limit the kernel raises kErrExchangeTimeout and returns (a rank that
+// never arrives cannot hang this GPU).
+#pragma once
+
+#include "common.cuh"
+
+namespace nnue {
+
+constexpr int kMaxCopies = 32;
+constexpr int kMaxRanks = 16;
+
+struct CopyDesc {
+  const float4* src;
+  float4* dst;
+  int64_t rows;
+  int64_t src_ld, dst_ld;  // row strides, in 16-byte vectors
+  int32_t width;           // 16-byte vectors per row
+  float scale;             // 1: the bytes are copied as they are
+};
+
+struct ExchangeParams {
+  CopyDesc c[kMaxCopies];
+  int64_t row_start[kMaxCopies + 1];  // prefix sums of rows over the copies
+  uint32_t* flags[kMaxRanks];         // rank s's flag words (n_ranks + 1 of them), mapped here
+  int32_t n_copies, n_ranks, rank;
+  uint32_t epoch;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// One warp per row (grid-stride over the rows of all copies), lanes over the
+// row's vectors.
+__global__ void __launch_bounds__(256) exchange_kernel(const __grid_constant__ ExchangeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t total = p.row_start[p.n_copies];
+  int i = 0;
+  for (int64_t g = warp; g < total; g += n_warps) {
+    while (i + 1 < p.n_copies && g >= p.row_start[i + 1]) ++i;  // rows only grow: the copy index only grows
+    const CopyDesc& c = p.c[i];
+    const int64_t r = g - p.row_start[i];
+    const float4* s = c.src + r * c.src_ld;
+    float4* d = c.dst + r * c.dst_ld;
+    if (c.scale == 1.f) {
+      for (int v = lane; v < c.width; v += 32) d[v] = __ldg(s + v);
+    } else {
+      const float k = c.scale;
+      for (int v = lane; v < c.width; v += 32) {
+        float4 x = __ldg(s + v);
+        x.x *= k;
+        x.y *= k;
+        x.z *= k;
+        x.w *= k;
+        d[v] = x;
+      }
+    }
+  }
+  // this block's stores, visible to every GPU before it counts itself done
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int s_last;
+  uint32_t* own = p.flags[p.rank];
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(own + p.n_ranks, 1u);
+    s_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x == 0) own[p.n_ranks] = 0;  // every block has counted: ready for the next launch
+  __threadfence_system();
+  if (threadIdx.x < p.n_ranks) st_release_sys(p.flags[threadIdx.x] + p.rank, p.epoch);
+  if (threadIdx.x < p.n_ranks) {
+    const uint64_t t0 = global_ns();
+    while ((int32_t)(ld_acquire_sys(own + threadIdx.x) - p.epoch) < 0) {
+      if (global_ns() - t0 > p.timeout_ns) {
+        flag_error(kErrExchangeTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+
+}  // namespace nnue

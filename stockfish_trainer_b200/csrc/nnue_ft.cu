@@ -23,6 +23,7 @@
 #include "ft_optim.cuh"
 #include "ft_quant.cuh"
 #include "ft_encode.cuh"
+#include "ft_exchange.cuh"
 
 namespace nnue {
 namespace {
@@ -1400,6 +1401,92 @@ int nnue_ft_backward_noalloc(const int32_t* idx0, const int32_t* idx1, int64_t b
   if (rc != NNUE_OK) return rc;
   return nnue_ft_backward(idx0, idx1, batch, max_active, grad0, grad1, n_persp, num_inputs, output_size, weight_grad,
                           bias_grad, accumulate, scratch, kNoAllocScratchBytes, stream);
+}
+
+// ---- exchange between the GPUs of one node --------------------------------
+int nnue_ft_exchange_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || bytes == 0) return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange_alloc: bad arguments");
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return check_launch("exchange_alloc: cudaMalloc");
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return check_launch("exchange_alloc: zeroing / IPC handle");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == NNUE_FT_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return NNUE_OK;
+}
+
+int nnue_ft_exchange_free(void* ptr) {
+  if (!ptr) return NNUE_OK;
+  if (cudaFree(ptr) != cudaSuccess) return check_launch("exchange_free");
+  return NNUE_OK;
+}
+
+int nnue_ft_exchange_open(const void* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  *ptr = nullptr;
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return check_launch("exchange_open: cudaIpcOpenMemHandle");
+  return NNUE_OK;
+}
+
+int nnue_ft_exchange_close(void* ptr) {
+  if (!ptr) return NNUE_OK;
+  if (cudaIpcCloseMemHandle(ptr) != cudaSuccess) return check_launch("exchange_close");
+  return NNUE_OK;
+}
+
+int nnue_ft_exchange(const nnue_ft_copy_desc* copies, int32_t n_copies, uint32_t* const* flags, int32_t n_ranks,
+                     int32_t rank, uint32_t epoch, int32_t timeout_ms, void* stream) {
+  if (n_copies < 0 || n_copies > kMaxCopies || (n_copies && !copies))
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: 0..%d copies", kMaxCopies);
+  if (!flags || n_ranks < 1 || n_ranks > kMaxRanks - 1 || rank < 0 || rank >= n_ranks || timeout_ms <= 0)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: bad group (1..%d ranks)", kMaxRanks - 1);
+  ExchangeParams p{};
+  p.n_copies = n_copies;
+  p.n_ranks = n_ranks;
+  p.rank = rank;
+  p.epoch = epoch;
+  p.timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+  for (int r = 0; r < n_ranks; ++r) {
+    if (!flags[r] || reinterpret_cast<uintptr_t>(flags[r]) % 4 != 0)
+      return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: flag words of rank %d null or misaligned", r);
+    p.flags[r] = flags[r];
+  }
+  int64_t rows = 0;
+  for (int i = 0; i < n_copies; ++i) {
+    const nnue_ft_copy_desc& c = copies[i];
+    if (c.rows < 0 || c.width < 0 || c.src_ld < c.width || c.dst_ld < c.width)
+      return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: copy %d has bad sizes", i);
+    if (c.rows > 0 && c.width > 0 && (!aligned16(c.src) || !aligned16(c.dst)))
+      return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: copy %d: null or not 16-byte aligned", i);
+    p.c[i].src = static_cast<const float4*>(c.src);
+    p.c[i].dst = static_cast<float4*>(c.dst);
+    p.c[i].rows = c.width > 0 ? c.rows : 0;
+    p.c[i].src_ld = c.src_ld;
+    p.c[i].dst_ld = c.dst_ld;
+    p.c[i].width = c.width;
+    p.c[i].scale = c.scale;
+    p.row_start[i] = rows;
+    rows += p.c[i].rows;
+  }
+  p.row_start[n_copies] = rows;
+  if (n_copies == 0) {  // a barrier only: one copy-less launch
+    p.c[0] = CopyDesc{};
+  }
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t warps_wanted = std::max<int64_t>(1, rows);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((int64_t)sms * 4, ceil_div(warps_wanted, 8)));
+  count_launch();
+  exchange_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("exchange");
 }
 
 int nnue_ft_gather_probe(const float* table, int64_t rows, const int32_t* idx, int32_t per_warp, int32_t n_warps,

@@ -6,9 +6,13 @@
   columns of the whole-table forward and backward.
 * One GPU, no process group: the autograd function equals
   SparseLinearPairFunction bit for bit.
-* Two GPUs (NCCL; skipped with fewer): each rank's outputs are its positions'
-  rows of the one-GPU forward, and its gradient columns are the one-GPU
-  full-batch gradient of those columns times 1/2, bit for bit."""
+* One GPU, the exchange kernel: strided, scaled and bit-for-bit copies with
+  the barrier of one rank; a barrier whose other rank never arrives times
+  out with the timeout flag instead of hanging.
+* Two GPUs (NCCL; skipped with fewer), both exchange paths: each rank's
+  outputs are its positions' rows of the one-GPU forward, and its gradient
+  columns are the one-GPU full-batch gradient of those columns times 1/2,
+  bit for bit."""
 
 import os
 import socket
@@ -73,15 +77,16 @@ def test_every_rank_slice_equals_whole_table_columns(cuda, world):
     assert _native.device_errors() == 0
 
 
-def test_single_process_equals_pair_function(cuda):
+@pytest.mark.parametrize("exchange", ["peer", "p2p"])
+def test_single_process_equals_pair_function(cuda, exchange):
     from stockfish_trainer_b200 import SparseLinearPairFunction, colsharded
 
     B, C = 2048, 264
     white, black, W, bias, g, T, K = _inputs(B, C, seed=9)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
     i0, i1 = t(white), t(black)
-    sh = colsharded.ColumnShardedFT(T, C, B, K, device=cuda)
-    assert (sh.world, sh.c0, sh.c1) == (1, 0, C)
+    sh = colsharded.ColumnShardedFT(T, C, B, K, device=cuda, exchange=exchange)
+    assert (sh.world, sh.c0, sh.c1, sh.exchange) == (1, 0, C, exchange)
     res = []
     for fn in (lambda a, b, w, c: SparseLinearPairFunction.apply(a, b, w, c),
                lambda a, b, w, c: colsharded.SparseLinearPairColumnSharded.apply(a, b, w, c, sh)):
@@ -92,9 +97,85 @@ def test_single_process_equals_pair_function(cuda):
     for a, b in zip(res[0][:3], res[1][:3]):
         assert torch.equal(a, b)
     torch.testing.assert_close(res[0][3], res[1][3], rtol=1e-5, atol=1e-6)
+    sh.close()
 
 
-def _worker(rank, world, port, out_dir, B, C):
+def _exchange_buffer(nbytes):
+    import ctypes
+
+    from stockfish_trainer_b200 import _native
+
+    p, h = ctypes.c_void_p(0), ctypes.create_string_buffer(64)
+    _native.call("nnue_ft_exchange_alloc", nbytes, ctypes.byref(p), h)
+    return p.value
+
+
+def test_exchange_copies_and_self_barrier(cuda):
+    """One rank: strided block copies (scaled, and bit-for-bit with scale 1,
+    int32 and NaN payloads included), then the barrier with itself; the flag
+    words count the epochs."""
+    import ctypes
+
+    from stockfish_trainer_b200 import _native, colsharded
+
+    buf = _exchange_buffer(1 << 20)
+    try:
+        flags = colsharded._device_view(buf, (16,), torch.int32, cuda)
+        assert int(flags.abs().sum()) == 0  # zeroed at allocation
+        rng = np.random.default_rng(3)
+        src = torch.from_numpy(rng.standard_normal((37, 24), dtype=np.float32)).to(cuda)
+        src[3, 10] = float("nan")  # inside the scale-1 copy
+        ints = torch.from_numpy(rng.integers(-2**31, 2**31 - 1, (37, 8), dtype=np.int64).astype(np.int32)).to(cuda)
+        dst = torch.full((37, 40), -7.0, device=cuda)
+        dst_i = torch.zeros(37, 8, dtype=torch.int32, device=cuda)
+        D = colsharded._CopyDesc
+        arr = (D * 3)(D(src.data_ptr() + 8 * 4, dst.data_ptr() + 4 * 4, 37, 6, 10, 3, 1.0),
+                      D(src.data_ptr(), dst.data_ptr() + 20 * 4, 37, 6, 10, 2, 0.25),
+                      D(ints.data_ptr(), dst_i.data_ptr(), 37, 2, 2, 2, 1.0))
+        fl = (ctypes.c_void_p * 1)(buf)
+        stream = torch.cuda.current_stream(cuda).cuda_stream
+        for epoch in (1, 2):
+            _native.call("nnue_ft_exchange", arr, 3, fl, 1, 0, epoch, 1000, stream)
+        torch.cuda.synchronize()
+        assert _native.device_errors() == 0
+        want = torch.full((37, 40), -7.0, device=cuda)
+        want[:, 4:16] = src[:, 8:20]
+        want[:, 20:28] = src[:, 0:8] * 0.25
+        got = dst.view(torch.int32)
+        assert torch.equal(got[:, :20], want.view(torch.int32)[:, :20])  # bit for bit, the NaN too
+        assert torch.equal(dst[:, 20:], want[:, 20:])
+        assert torch.equal(dst_i, ints)
+        assert flags[0].item() == 2 and flags[1].item() == 0  # epoch 2 seen; the block counter reset
+    finally:
+        _native.call("nnue_ft_exchange_free", buf)
+
+
+def test_exchange_barrier_times_out_without_the_other_rank(cuda):
+    """Two ranks' flag words, one process playing rank 0: rank 1 never
+    signals, so the bounded wait runs out, raises the timeout flag and the
+    launch returns; the context stays usable."""
+    import ctypes
+    import time
+
+    from stockfish_trainer_b200 import _native
+
+    own, other = _exchange_buffer(4096), _exchange_buffer(4096)
+    try:
+        fl = (ctypes.c_void_p * 2)(own, other)
+        _native.device_errors()  # start from clear flags
+        t0 = time.perf_counter()
+        _native.call("nnue_ft_exchange", None, 0, fl, 2, 0, 1, 200, torch.cuda.current_stream(cuda).cuda_stream)
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 >= 0.19
+        assert _native.device_errors() == _native.DEVERR_EXCHANGE_TIMEOUT
+        x = torch.ones(8, device=cuda)
+        assert float((x * 2).sum()) == 16.0
+    finally:
+        _native.call("nnue_ft_exchange_free", own)
+        _native.call("nnue_ft_exchange_free", other)
+
+
+def _worker(rank, world, port, out_dir, B, C, exchange):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
@@ -106,7 +187,8 @@ def _worker(rank, world, port, out_dir, B, C):
     b = B // world
     lo = rank * b
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-    sh = colsharded.ColumnShardedFT(T, C, B, K, device=dev)
+    sh = colsharded.ColumnShardedFT(T, C, B, K, device=dev, exchange=exchange)
+    assert sh.exchange == exchange
     Wp = sh.shard_columns(t(W)).requires_grad_()
     bp = sh.shard_columns(t(bias)).requires_grad_()
     for _ in range(2):  # two steps: the second reuses every buffer
@@ -115,19 +197,23 @@ def _worker(rank, world, port, out_dir, B, C):
         torch.autograd.backward([o0, o1], [t(g[0, lo:lo + b]), t(g[1, lo:lo + b])])
     full = sh.gather_columns(Wp.grad)
     torch.cuda.synchronize()
+    from stockfish_trainer_b200 import _native
+
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), o0=o0.detach().cpu().numpy(), o1=o1.detach().cpu().numpy(),
-             dW=Wp.grad.cpu().numpy(), dB=bp.grad.cpu().numpy(), c0=sh.c0, c1=sh.c1, full=full.cpu().numpy())
+             dW=Wp.grad.cpu().numpy(), dB=bp.grad.cpu().numpy(), c0=sh.c0, c1=sh.c1, full=full.cpu().numpy(),
+             errors=_native.device_errors())
+    sh.close()
     torch.distributed.barrier()
     torch.distributed.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("C", [1048, 264])
-def test_two_gpu_column_sharded_matches_one_gpu(tmp_path, C):
+@pytest.mark.parametrize("C,exchange", [(1048, "peer"), (264, "peer"), (1048, "p2p")])
+def test_two_gpu_column_sharded_matches_one_gpu(tmp_path, C, exchange):
     from stockfish_trainer_b200.feature_transformer import ops
 
     world, B = 2, 4096
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), B, C), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), B, C, exchange), nprocs=world, join=True,
                        start_method="spawn")
     white, black, W, bias, g, T, K = _inputs(B, C)
     dev = torch.device("cuda", 0)
@@ -141,6 +227,7 @@ def test_two_gpu_column_sharded_matches_one_gpu(tmp_path, C):
     b = B // world
     for r in range(world):
         z = np.load(tmp_path / f"r{r}.npz")
+        assert int(z["errors"]) == 0
         c0, c1 = int(z["c0"]), int(z["c1"])
         np.testing.assert_array_equal(z["o0"], o0[r * b:(r + 1) * b])
         np.testing.assert_array_equal(z["o1"], o1[r * b:(r + 1) * b])

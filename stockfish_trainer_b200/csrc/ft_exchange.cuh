@@ -56,31 +56,53 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// One warp per row (grid-stride over the rows of all copies), lanes over the
-// row's vectors.
+// Warps take R consecutive rows at a time (grid-stride over the rows of all
+// copies), lanes over the rows' vectors: all R rows' loads are issued before
+// their stores, so R loads per lane are in flight.
+template <int R>
 __global__ void __launch_bounds__(256) exchange_kernel(const __grid_constant__ ExchangeParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t total = p.row_start[p.n_copies];
-  int i = 0;
-  for (int64_t g = warp; g < total; g += n_warps) {
-    while (i + 1 < p.n_copies && g >= p.row_start[i + 1]) ++i;  // rows only grow: the copy index only grows
-    const CopyDesc& c = p.c[i];
-    const int64_t r = g - p.row_start[i];
-    const float4* s = c.src + r * c.src_ld;
-    float4* d = c.dst + r * c.dst_ld;
-    if (c.scale == 1.f) {
-      for (int v = lane; v < c.width; v += 32) d[v] = __ldg(s + v);
-    } else {
-      const float k = c.scale;
-      for (int v = lane; v < c.width; v += 32) {
-        float4 x = __ldg(s + v);
-        x.x *= k;
-        x.y *= k;
-        x.z *= k;
-        x.w *= k;
-        d[v] = x;
+  int i = 0;  // copy of the first row of the group; rows only grow, so it only grows
+  for (int64_t g0 = warp * R; g0 < total; g0 += n_warps * R) {
+    while (i + 1 < p.n_copies && g0 >= p.row_start[i + 1]) ++i;
+    const float4* src[R];
+    float4* dst[R];
+    int width[R];
+    float scale[R];
+    int maxw = 0;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int64_t g = g0 + j;
+      int k = i;
+      while (k + 1 < p.n_copies && g >= p.row_start[k + 1]) ++k;
+      const bool live = g < total;
+      const CopyDesc& c = p.c[k];
+      const int64_t r = g - p.row_start[k];
+      src[j] = c.src + (live ? r * c.src_ld : 0);
+      dst[j] = c.dst + (live ? r * c.dst_ld : 0);
+      width[j] = live ? c.width : 0;
+      scale[j] = c.scale;
+      maxw = max(maxw, width[j]);
+    }
+    for (int v0 = 0; v0 < maxw; v0 += 32) {
+      const int v = v0 + lane;
+      float4 x[R];
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (v < width[j]) x[j] = __ldg(src[j] + v);
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        if (v >= width[j]) continue;
+        if (scale[j] != 1.f) {
+          x[j].x *= scale[j];
+          x[j].y *= scale[j];
+          x[j].z *= scale[j];
+          x[j].w *= scale[j];
+        }
+        dst[j][v] = x[j];
       }
     }
   }

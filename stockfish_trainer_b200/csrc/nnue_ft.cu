@@ -121,6 +121,13 @@ struct Tuning {
   // items, 1.5% slower at 2 x 8192).
   int64_t fwd_tail = 3;
   int64_t bwd_tail = 2;
+  // order of the backward's side-stream work: 0 = packed tail chunk, heavy rows, bias sum; 1 = heavy rows
+  // first (the heavy rows' long sequential walks start at once: the longest side-stream task when the light
+  // rows are short, as on a narrow column slice)
+  int64_t bwd_heavy_first = 0;
+  // exchange kernel: rows each warp copies at once (1, 2 or 4) and resident blocks per SM (grid size)
+  int64_t xchg_rows = 1;
+  int64_t xchg_blocks_per_sm = 4;
 };
 Tuning g_tune;
 
@@ -154,6 +161,9 @@ ParamRef* params() {
       {"fwd_queue_blocks", &g_tune.fwd_queue_blocks, 8, 16},
       {"fwd_tail", &g_tune.fwd_tail, 0, 3},
       {"bwd_tail", &g_tune.bwd_tail, 0, 2},
+      {"bwd_heavy_first", &g_tune.bwd_heavy_first, 0, 1},
+      {"xchg_rows", &g_tune.xchg_rows, 1, 4},
+      {"xchg_blocks_per_sm", &g_tune.xchg_blocks_per_sm, 1, 16},
       {nullptr, nullptr, 0, 0},
   };
   return p;
@@ -802,7 +812,8 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
     if (cudaEventRecord(aux->fork, s) != cudaSuccess || cudaStreamWaitEvent(aux->side, aux->fork, 0) != cudaSuccess)
       return check_launch("backward_apply: fork");
     // bwd_tail 2: the light rows' packed last chunk here, beside the main light-row kernel
-    if (rows && v4 && g_tune.bwd_tail == 2) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
+    const bool tail_here = rows && v4 && g_tune.bwd_tail == 2;
+    if (tail_here && !g_tune.bwd_heavy_first) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
     if (rows) {
       if (pl.P == 2 && pl.heavy_cap > 0 &&
           cudaMemsetAsync(w.hticket, 0, sizeof(uint32_t) * pl.heavy_cap * p.g.n_vec, aux->side) != cudaSuccess)
@@ -810,6 +821,7 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
       rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
       if (rc != NNUE_OK) return rc;
     }
+    if (tail_here && g_tune.bwd_heavy_first) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
     if (with_bias) launch_colsum(g0, g1, pl, v4, w.partial, dB, p.accumulate, aux->side);
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
   }
@@ -1482,10 +1494,15 @@ int nnue_ft_exchange(const nnue_ft_copy_desc* copies, int32_t n_copies, uint32_t
   }
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t warps_wanted = std::max<int64_t>(1, rows);
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((int64_t)sms * 4, ceil_div(warps_wanted, 8)));
+  const int R = g_tune.xchg_rows >= 4 ? 4 : g_tune.xchg_rows >= 2 ? 2 : 1;
+  const int64_t warps_wanted = std::max<int64_t>(1, ceil_div(rows, R));
+  const unsigned grid = (unsigned)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)sms * g_tune.xchg_blocks_per_sm, ceil_div(warps_wanted, 8)));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
   count_launch();
-  exchange_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  if (R == 4) exchange_kernel<4><<<grid, 256, 0, st>>>(p);
+  else if (R == 2) exchange_kernel<2><<<grid, 256, 0, st>>>(p);
+  else exchange_kernel<1><<<grid, 256, 0, st>>>(p);
   return check_launch("exchange");
 }
 

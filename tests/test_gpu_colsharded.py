@@ -110,15 +110,19 @@ def _exchange_buffer(nbytes):
     return p.value
 
 
-def test_exchange_copies_and_self_barrier(cuda):
+@pytest.mark.parametrize("rows,blocks", [(1, 4), (2, 1), (4, 8)])
+def test_exchange_copies_and_self_barrier(cuda, rows, blocks):
     """One rank: strided block copies (scaled, and bit-for-bit with scale 1,
     int32 and NaN payloads included), then the barrier with itself; the flag
-    words count the epochs."""
+    words count the epochs.  Every rows-per-warp / grid setting."""
     import ctypes
 
     from stockfish_trainer_b200 import _native, colsharded
 
     buf = _exchange_buffer(1 << 20)
+    old = {k: _native.get_param(k) for k in ("xchg_rows", "xchg_blocks_per_sm")}
+    _native.set_param("xchg_rows", rows)
+    _native.set_param("xchg_blocks_per_sm", blocks)
     try:
         flags = colsharded._device_view(buf, (16,), torch.int32, cuda)
         assert int(flags.abs().sum()) == 0  # zeroed at allocation
@@ -147,6 +151,8 @@ def test_exchange_copies_and_self_barrier(cuda):
         assert torch.equal(dst_i, ints)
         assert flags[0].item() == 2 and flags[1].item() == 0  # epoch 2 seen; the block counter reset
     finally:
+        for k, v in old.items():
+            _native.set_param(k, v)
         _native.call("nnue_ft_exchange_free", buf)
 
 

@@ -121,9 +121,10 @@ struct Tuning {
   // items, 1.5% slower at 2 x 8192).
   int64_t fwd_tail = 3;
   int64_t bwd_tail = 2;
-  // order of the backward's side-stream work: 0 = packed tail chunk, heavy rows, bias sum; 1 = heavy rows
-  // first (the heavy rows' long sequential walks start at once: the longest side-stream task when the light
-  // rows are short, as on a narrow column slice)
+  // where the heavy rows run: 0 = on the side stream after the packed tail chunk, beside the light rows;
+  // 1 = the same, before the tail chunk (their long sequential walks start at once: the longest side-stream
+  // task when the light rows are short, as on a narrow column slice); 2 = alone on the caller's stream before
+  // the light rows (beside 64 light warps per SM each heavy warp gets a small share of the issue slots)
   int64_t bwd_heavy_first = 0;
   // exchange kernel: rows each warp copies at once (1, 2 or 4) and resident blocks per SM (grid size)
   int64_t xchg_rows = 1;
@@ -161,7 +162,7 @@ ParamRef* params() {
       {"fwd_queue_blocks", &g_tune.fwd_queue_blocks, 8, 16},
       {"fwd_tail", &g_tune.fwd_tail, 0, 3},
       {"bwd_tail", &g_tune.bwd_tail, 0, 2},
-      {"bwd_heavy_first", &g_tune.bwd_heavy_first, 0, 1},
+      {"bwd_heavy_first", &g_tune.bwd_heavy_first, 0, 2},
       {"xchg_rows", &g_tune.xchg_rows, 1, 4},
       {"xchg_blocks_per_sm", &g_tune.xchg_blocks_per_sm, 1, 16},
       {nullptr, nullptr, 0, 0},
@@ -806,6 +807,16 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
   DeviceAux* aux = nullptr;
   int rc = device_aux(&aux);
   if (rc != NNUE_OK) return rc;
+  auto launch_heavy = [&](cudaStream_t hs) -> int {
+    if (pl.P == 2 && pl.heavy_cap > 0 &&
+        cudaMemsetAsync(w.hticket, 0, sizeof(uint32_t) * pl.heavy_cap * p.g.n_vec, hs) != cudaSuccess)
+      return check_launch("backward_apply: heavy tickets");
+    return v4 ? launch_segsum_heavy<float4>(p, hs) : launch_segsum_heavy<float>(p, hs);
+  };
+  // bwd_heavy_first 2: the heavy rows alone on the caller's stream first -- their warps then get the
+  // issue slots the light rows' 64 warps per SM would otherwise share with them
+  const bool heavy_alone = rows && g_tune.bwd_heavy_first == 2;
+  if (heavy_alone && (rc = launch_heavy(s)) != NNUE_OK) return rc;
   {
     // fork: heavy rows and the bias column sum on the side stream
     std::lock_guard<std::mutex> lock(g_aux_mu);
@@ -813,15 +824,9 @@ int apply_impl(const float* g0, const float* g1, const BwdPlan& pl, const Ws& w,
       return check_launch("backward_apply: fork");
     // bwd_tail 2: the light rows' packed last chunk here, beside the main light-row kernel
     const bool tail_here = rows && v4 && g_tune.bwd_tail == 2;
-    if (tail_here && !g_tune.bwd_heavy_first) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
-    if (rows) {
-      if (pl.P == 2 && pl.heavy_cap > 0 &&
-          cudaMemsetAsync(w.hticket, 0, sizeof(uint32_t) * pl.heavy_cap * p.g.n_vec, aux->side) != cudaSuccess)
-        return check_launch("backward_apply: heavy tickets");
-      rc = v4 ? launch_segsum_heavy<float4>(p, aux->side) : launch_segsum_heavy<float>(p, aux->side);
-      if (rc != NNUE_OK) return rc;
-    }
-    if (tail_here && g_tune.bwd_heavy_first) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
+    if (tail_here && g_tune.bwd_heavy_first != 1) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
+    if (rows && !heavy_alone && (rc = launch_heavy(aux->side)) != NNUE_OK) return rc;
+    if (tail_here && g_tune.bwd_heavy_first == 1) tail_done = launch_segsum_tail(p, delta_ok, aux->side);
     if (with_bias) launch_colsum(g0, g1, pl, v4, w.partial, dB, p.accumulate, aux->side);
     if (cudaEventRecord(aux->join, aux->side) != cudaSuccess) return check_launch("backward_apply: join record");
   }

@@ -121,6 +121,10 @@ def _with_params(params, fn):
         {"bwd_queue": 2, "heavy_threshold": 10**9, "bwd_queue_min_entries": 0},  # hot rows on the queued path
         {"bwd_queue": 6, "bwd_queue_min_blocks": 8, "bwd_chunk_vec": 8, "bwd_queue_min_entries": 0},
         {"bwd_queue": 2, "bwd_queue_min_entries": 10**9},  # the heuristic picks the batched kernel
+        # heavy rows before the packed tail chunk on the side stream, and alone on the caller's stream
+        {"bwd_heavy_first": 1, "heavy_threshold": 4, "heavy_cap": 40},
+        {"bwd_heavy_first": 2, "heavy_threshold": 4, "heavy_cap": 40},
+        {"bwd_heavy_first": 2, "bwd_tail": 1, "heavy_threshold": 4, "heavy_cap": 3},
     ],
 )
 def test_backward_tuning_and_heavy_rows(cuda, params):

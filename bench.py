@@ -92,6 +92,8 @@ def parse_args():
     p.add_argument("--exchange", choices=["peer", "p2p"], default=None,
                    help="--parallel cols: peer = this library's exchange kernel storing into the other GPUs' "
                         "buffers (the default), p2p = torch.distributed point-to-point operations")
+    p.add_argument("--cols-prepare", choices=["forward", "overlap"], default="forward",
+                   help="--parallel cols: where the backward's index phase runs (colsharded.ColumnShardedFT)")
     p.add_argument("--ddp-blocks", type=int, default=4,
                    help="N > 1: row blocks whose gradient allreduce overlaps the next block's backward "
                         "(0 = one allreduce after the whole backward)")
@@ -473,7 +475,8 @@ def run_ours(args):
         # every position of the global batch
         from stockfish_trainer_b200 import colsharded
 
-        plan = colsharded.ColumnShardedFT(T, C, args.batch, K, device=dev, exchange=args.exchange)
+        plan = colsharded.ColumnShardedFT(T, C, args.batch, K, device=dev, exchange=args.exchange,
+                                          prepare=args.cols_prepare)
         Wk, bk, kc, kb = plan.shard_columns(W), plan.shard_columns(bias), plan.width, args.batch
         W = None  # this rank keeps its columns only
         ws = plan.workspace
@@ -966,7 +969,8 @@ def run_ours(args):
             "dtype": "f32",
             "data": DATA,
             "config": dict(base_config(args, world, b_rank, T, K, int(nnz_all)),
-                           **({"exchange": plan.exchange, "column_slices": plan.slices} if cols else {})),
+                           **({"exchange": plan.exchange, "column_slices": plan.slices,
+                               "index_phase": plan.prepare} if cols else {})),
             "phases_ms": phase_ms,
             "instrumented_ms_per_step": ms_instrumented,
             "roofline": roofline,

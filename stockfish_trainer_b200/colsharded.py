@@ -148,6 +148,18 @@ class _CudaKernels:
         ops.forward_pair_prepare(idx0, idx1, weight, bias, out0, out1, workspace)
 
     @staticmethod
+    def forward(idx0, idx1, weight, bias, out0, out1):
+        from .feature_transformer import ops
+
+        ops.forward_pair_into(idx0, idx1, weight, bias, out0, out1)
+
+    @staticmethod
+    def prepare(idx0, idx1, num_inputs, width, workspace):
+        from .feature_transformer import ops
+
+        ops.backward_prepare(idx0, idx1, num_inputs, width, workspace)
+
+    @staticmethod
     def backward_apply(grad0, grad1, batch, max_active, weight_grad, bias_grad, workspace):
         from .feature_transformer import ops
 
@@ -177,10 +189,15 @@ class ColumnShardedFT:
     the blocks with torch ops.  With "peer" the returned outputs live in the
     exchange buffer, two steps' worth: a step's outputs stay valid until the
     forward after the next one.  Call ``close`` on every rank (it is a
-    collective) before the process group goes away."""
+    collective) before the process group goes away.
+
+    ``prepare``: "forward" runs the backward's index phase beside the forward
+    on the library's high-priority side stream (as one GPU does); "overlap"
+    runs it on a normal-priority stream of its own, so the forward's gathers
+    come first and the index phase continues through the exchanges."""
 
     def __init__(self, num_inputs: int, output_size: int, batch: int, max_active: int, device=None, group=None,
-                 kernels=None, exchange: Optional[str] = None, timeout_ms: int = 5000):
+                 kernels=None, exchange: Optional[str] = None, timeout_ms: int = 5000, prepare: str = "forward"):
         self.group = group
         self.timeout_ms = int(timeout_ms)
         dist_on = dist.is_available() and dist.is_initialized()
@@ -198,6 +215,13 @@ class ColumnShardedFT:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         dev = self.device
         self.scale = 1.0 / self.world
+        if prepare not in ("forward", "overlap"):
+            raise ValueError(f"prepare must be 'forward' or 'overlap', got {prepare!r}")
+        self.prepare = prepare
+        self._prep_stream = self._prep_done = None
+        if prepare == "overlap" and dev.type == "cuda":
+            self._prep_stream = torch.cuda.Stream(device=dev)  # normal priority
+            self._prep_done = torch.cuda.Event()
         # this rank's columns of every position's output
         self.y = torch.empty(2, self.B, self.width, device=dev)
         self.workspace = self.kernels.alloc_workspace(self.B, self.K, self.T, self.width, dev)
@@ -380,8 +404,19 @@ class ColumnShardedFT:
         (``gather_indices`` first) on this rank's columns."""
         if tuple(weight_cols.shape) != (self.T, self.width) or tuple(bias_cols.shape) != (self.width,):
             raise ValueError(f"this rank's parameters must be [{self.T}, {self.width}] and [{self.width}]")
-        self.kernels.forward_prepare(self.idx[0], self.idx[1], weight_cols, bias_cols, self.y[0], self.y[1],
-                                     self.workspace)
+        if self._prep_stream is None:
+            self.kernels.forward_prepare(self.idx[0], self.idx[1], weight_cols, bias_cols, self.y[0], self.y[1],
+                                         self.workspace)
+            return
+        # the index phase on its own normal-priority stream: the forward's
+        # gathers take the SMs first, the index phase fills what they leave
+        # and runs on into the exchanges; backward_local waits for it
+        cur = torch.cuda.current_stream(self.device)
+        self._prep_stream.wait_stream(cur)
+        with torch.cuda.stream(self._prep_stream):
+            self.kernels.prepare(self.idx[0], self.idx[1], self.T, self.width, self.workspace)
+            self._prep_done.record(self._prep_stream)
+        self.kernels.forward(self.idx[0], self.idx[1], weight_cols, bias_cols, self.y[0], self.y[1])
 
     def exchange_outputs(self, out0: Optional[torch.Tensor] = None, out1: Optional[torch.Tensor] = None):
         """Rank s receives rows [s*b, (s+1)*b) of every rank's columns; each
@@ -457,6 +492,8 @@ class ColumnShardedFT:
     def backward_local(self, weight_grad_cols: torch.Tensor, bias_grad_cols: torch.Tensor) -> None:
         """The segment sums over all positions on this rank's columns (after
         ``exchange_grads``; needs the workspace of ``forward_local``)."""
+        if self._prep_done is not None:
+            torch.cuda.current_stream(self.device).wait_event(self._prep_done)
         self.kernels.backward_apply(self.d[0], self.d[1], self.B, self.K, weight_grad_cols, bias_grad_cols,
                                     self.workspace)
 

@@ -77,15 +77,15 @@ def test_every_rank_slice_equals_whole_table_columns(cuda, world):
     assert _native.device_errors() == 0
 
 
-@pytest.mark.parametrize("exchange", ["peer", "p2p"])
-def test_single_process_equals_pair_function(cuda, exchange):
+@pytest.mark.parametrize("exchange,prepare", [("peer", "forward"), ("p2p", "forward"), ("peer", "overlap")])
+def test_single_process_equals_pair_function(cuda, exchange, prepare):
     from stockfish_trainer_b200 import SparseLinearPairFunction, colsharded
 
     B, C = 2048, 264
     white, black, W, bias, g, T, K = _inputs(B, C, seed=9)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
     i0, i1 = t(white), t(black)
-    sh = colsharded.ColumnShardedFT(T, C, B, K, device=cuda, exchange=exchange)
+    sh = colsharded.ColumnShardedFT(T, C, B, K, device=cuda, exchange=exchange, prepare=prepare)
     assert (sh.world, sh.c0, sh.c1, sh.exchange) == (1, 0, C, exchange)
     res = []
     for fn in (lambda a, b, w, c: SparseLinearPairFunction.apply(a, b, w, c),
@@ -181,7 +181,7 @@ def test_exchange_barrier_times_out_without_the_other_rank(cuda):
         _native.call("nnue_ft_exchange_free", other)
 
 
-def _worker(rank, world, port, out_dir, B, C, exchange):
+def _worker(rank, world, port, out_dir, B, C, exchange, prepare):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
@@ -193,7 +193,7 @@ def _worker(rank, world, port, out_dir, B, C, exchange):
     b = B // world
     lo = rank * b
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-    sh = colsharded.ColumnShardedFT(T, C, B, K, device=dev, exchange=exchange)
+    sh = colsharded.ColumnShardedFT(T, C, B, K, device=dev, exchange=exchange, prepare=prepare)
     assert sh.exchange == exchange
     Wp = sh.shard_columns(t(W)).requires_grad_()
     bp = sh.shard_columns(t(bias)).requires_grad_()
@@ -214,13 +214,14 @@ def _worker(rank, world, port, out_dir, B, C, exchange):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("C,exchange", [(1048, "peer"), (264, "peer"), (1048, "p2p")])
-def test_two_gpu_column_sharded_matches_one_gpu(tmp_path, C, exchange):
+@pytest.mark.parametrize("C,exchange,prepare", [(1048, "peer", "forward"), (264, "peer", "overlap"),
+                                                (1048, "p2p", "forward")])
+def test_two_gpu_column_sharded_matches_one_gpu(tmp_path, C, exchange, prepare):
     from stockfish_trainer_b200.feature_transformer import ops
 
     world, B = 2, 4096
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), B, C, exchange), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), B, C, exchange, prepare), nprocs=world,
+                       join=True, start_method="spawn")
     white, black, W, bias, g, T, K = _inputs(B, C)
     dev = torch.device("cuda", 0)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)

@@ -366,9 +366,11 @@ int nnue_ft_encode_features(const uint8_t *board, int64_t count, int32_t feature
  * (nnue_ft_exchange_alloc, an exception to "nothing here allocates": a
  * buffer of its own, so its IPC handle maps exactly it), shares the handle
  * with the other ranks of the node (any host channel) and maps theirs
- * (nnue_ft_exchange_open).  The buffer's first 64 bytes are the rank's flag
- * words (zeroed at allocation); the rest is the caller's. */
+ * (nnue_ft_exchange_open).  The buffer's first NNUE_FT_EXCHANGE_FLAG_BYTES
+ * are the rank's flag words (zeroed at allocation); the rest is the
+ * caller's. */
 #define NNUE_FT_IPC_HANDLE_BYTES 64
+#define NNUE_FT_EXCHANGE_FLAG_BYTES 256 /* the flag words at the start of an exchange buffer */
 
 /* cudaMalloc'd + zeroed buffer of `bytes` and its CUDA IPC handle
  * (NNUE_FT_IPC_HANDLE_BYTES bytes).  Synchronous.  Free with
@@ -396,17 +398,19 @@ typedef struct {
 } nnue_ft_copy_desc;
 
 /* Runs up to 32 copies in one launch, then a barrier of the n_ranks (<= 15)
- * ranks: flags[s] = rank s's flag words (its exchange buffer's start, mapped
- * here; flags[rank] = this rank's own).  Every rank calls it in the same
- * order with the same epoch, which must grow by one per call (the first
- * call after allocation uses 1).  When the launch completes on this
- * rank's stream, every rank's copies of this epoch are done and visible.
+ * ranks on `channel` (0..3; independent barriers, so exchanges on different
+ * streams may be in flight together, one channel each): flags[s] = rank s's
+ * flag words (its exchange buffer's start, mapped here; flags[rank] = this
+ * rank's own).  Every rank calls it on a channel in the same order with the
+ * same epoch, which grows by one per call on that channel (the first call
+ * after allocation uses 1).  When the launch completes on this rank's
+ * stream, every rank's copies of this epoch are done and visible.
  * A rank that does not arrive within timeout_ms raises
  * NNUE_DEVERR_EXCHANGE_TIMEOUT and the launch returns without it (the
  * exchanged data is then incomplete).  Not capturable in a CUDA graph
  * (the epoch is a launch argument).  n_copies == 0: the barrier alone. */
 int nnue_ft_exchange(const nnue_ft_copy_desc *copies, int32_t n_copies, uint32_t *const *flags, int32_t n_ranks,
-                     int32_t rank, uint32_t epoch, int32_t timeout_ms, void *stream);
+                     int32_t rank, int32_t channel, uint32_t epoch, int32_t timeout_ms, void *stream);
 
 #ifdef __cplusplus
 }

@@ -72,7 +72,7 @@ _SIGNATURES = {
     "nnue_ft_exchange_free": (_I32, [_P]),
     "nnue_ft_exchange_open": (_I32, [_P, ctypes.POINTER(_P)]),
     "nnue_ft_exchange_close": (_I32, [_P]),
-    "nnue_ft_exchange": (_I32, [_P, _I32, _P, _I32, _I32, ctypes.c_uint32, _I32, _P]),
+    "nnue_ft_exchange": (_I32, [_P, _I32, _P, _I32, _I32, _I32, ctypes.c_uint32, _I32, _P]),
 }
 
 _lib = None

@@ -288,7 +288,7 @@ class ColumnShardedFT:
                 _native.call("nnue_ft_exchange_open", ctypes.create_string_buffer(h, 64), ctypes.byref(p))
                 bases.append(p.value)
         self._peer = {"base": bases, "own": base.value, "off_idx": off_idx, "off_out": off_out, "off_d": off_d,
-                      "epoch": 0, "flags": (ctypes.c_void_p * self.world)(*bases), "total": total}
+                      "epoch": [0, 0, 0, 0], "flags": (ctypes.c_void_p * self.world)(*bases), "total": total}
         own = base.value
         self.idx = _device_view(own + off_idx, (2, self.B, self.K), torch.int32, self.device)
         self._out = [_device_view(own + off_out + i * 2 * self.b * self.C * f32, (2, self.b, self.C), torch.float32,
@@ -315,9 +315,9 @@ class ColumnShardedFT:
         self._peer = None
         self.idx = self.d = self._out = None
 
-    def _peer_exchange(self, copies) -> None:
+    def _peer_exchange(self, copies, channel: int = 0) -> None:
         """copies: [(src_ptr, dst_ptr, rows, src_ld, dst_ld, width, scale)],
-        strides and widths in 16-byte vectors."""
+        strides and widths in 16-byte vectors; on the current stream."""
         import ctypes
 
         from . import _native
@@ -325,11 +325,12 @@ class ColumnShardedFT:
         arr = (_CopyDesc * max(len(copies), 1))()
         for i, (src, dst, rows, sld, dld, w, sc) in enumerate(copies):
             arr[i] = _CopyDesc(src, dst, rows, sld, dld, w, sc)
-        self._peer["epoch"] += 1
+        ep = self._peer["epoch"]
+        ep[channel] += 1
         with torch.cuda.device(self.device):
             stream = torch.cuda.current_stream(self.device).cuda_stream
-            _native.call("nnue_ft_exchange", arr, len(copies), self._peer["flags"], self.world, self.rank,
-                         self._peer["epoch"] & 0xFFFFFFFF, self.timeout_ms, stream)
+            _native.call("nnue_ft_exchange", arr, len(copies), self._peer["flags"], self.world, self.rank, channel,
+                         ep[channel] & 0xFFFFFFFF, self.timeout_ms, stream)
 
     # -- parameters ---------------------------------------------------------
     def shard_columns(self, full: torch.Tensor) -> torch.Tensor:

@@ -4,7 +4,9 @@
 // among the ranks of the group through flag words in each rank's exchange
 // buffer.
 //
-// Every rank launches the same sequence of exchanges with the same epoch.
+// Every rank launches the same sequence of exchanges on each channel with the
+// same epochs (channels are independent barriers, so exchanges on different
+// streams may be in flight at once, one channel each).
 // One launch: all blocks copy their rows; each block then makes its stores
 // visible system-wide (fence.sc.sys) and counts itself done; the last block
 // writes `epoch` into flag[rank] of every rank (st.release.sys) and waits
@@ -31,10 +33,12 @@ struct CopyDesc {
   float scale;             // 1: the bytes are copied as they are
 };
 
+constexpr int kChannels = 4;  // independent barriers: kMaxRanks flag words each (the last one the block counter)
+
 struct ExchangeParams {
   CopyDesc c[kMaxCopies];
   int64_t row_start[kMaxCopies + 1];  // prefix sums of rows over the copies
-  uint32_t* flags[kMaxRanks];         // rank s's flag words (n_ranks + 1 of them), mapped here
+  uint32_t* flags[kMaxRanks];         // rank s's flag words of this launch's channel, mapped here
   int32_t n_copies, n_ranks, rank;
   uint32_t epoch;
   uint64_t timeout_ns;
@@ -112,12 +116,12 @@ __global__ void __launch_bounds__(256) exchange_kernel(const __grid_constant__ E
   __shared__ int s_last;
   uint32_t* own = p.flags[p.rank];
   if (threadIdx.x == 0) {
-    const uint32_t prev = atomicAdd(own + p.n_ranks, 1u);
+    const uint32_t prev = atomicAdd(own + (kMaxRanks - 1), 1u);
     s_last = prev == gridDim.x - 1;
   }
   __syncthreads();
   if (!s_last) return;
-  if (threadIdx.x == 0) own[p.n_ranks] = 0;  // every block has counted: ready for the next launch
+  if (threadIdx.x == 0) own[kMaxRanks - 1] = 0;  // every block has counted: ready for the next launch
   __threadfence_system();
   if (threadIdx.x < p.n_ranks) st_release_sys(p.flags[threadIdx.x] + p.rank, p.epoch);
   if (threadIdx.x < p.n_ranks) {

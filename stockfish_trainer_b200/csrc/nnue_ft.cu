@@ -1460,11 +1460,14 @@ int nnue_ft_exchange_close(void* ptr) {
 }
 
 int nnue_ft_exchange(const nnue_ft_copy_desc* copies, int32_t n_copies, uint32_t* const* flags, int32_t n_ranks,
-                     int32_t rank, uint32_t epoch, int32_t timeout_ms, void* stream) {
+                     int32_t rank, int32_t channel, uint32_t epoch, int32_t timeout_ms, void* stream) {
   if (n_copies < 0 || n_copies > kMaxCopies || (n_copies && !copies))
     return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: 0..%d copies", kMaxCopies);
   if (!flags || n_ranks < 1 || n_ranks > kMaxRanks - 1 || rank < 0 || rank >= n_ranks || timeout_ms <= 0)
     return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: bad group (1..%d ranks)", kMaxRanks - 1);
+  if (channel < 0 || channel >= kChannels)
+    return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: channel %d outside [0, %d)", (int)channel, kChannels);
+  static_assert(kChannels * kMaxRanks * sizeof(uint32_t) <= NNUE_FT_EXCHANGE_FLAG_BYTES, "flag words");
   ExchangeParams p{};
   p.n_copies = n_copies;
   p.n_ranks = n_ranks;
@@ -1474,7 +1477,7 @@ int nnue_ft_exchange(const nnue_ft_copy_desc* copies, int32_t n_copies, uint32_t
   for (int r = 0; r < n_ranks; ++r) {
     if (!flags[r] || reinterpret_cast<uintptr_t>(flags[r]) % 4 != 0)
       return fail(NNUE_ERR_INVALID_ARGUMENT, "exchange: flag words of rank %d null or misaligned", r);
-    p.flags[r] = flags[r];
+    p.flags[r] = flags[r] + channel * kMaxRanks;
   }
   int64_t rows = 0;
   for (int i = 0; i < n_copies; ++i) {

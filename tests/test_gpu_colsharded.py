@@ -124,7 +124,7 @@ def test_exchange_copies_and_self_barrier(cuda, rows, blocks):
     _native.set_param("xchg_rows", rows)
     _native.set_param("xchg_blocks_per_sm", blocks)
     try:
-        flags = colsharded._device_view(buf, (16,), torch.int32, cuda)
+        flags = colsharded._device_view(buf, (64,), torch.int32, cuda)
         assert int(flags.abs().sum()) == 0  # zeroed at allocation
         rng = np.random.default_rng(3)
         src = torch.from_numpy(rng.standard_normal((37, 24), dtype=np.float32)).to(cuda)
@@ -139,7 +139,8 @@ def test_exchange_copies_and_self_barrier(cuda, rows, blocks):
         fl = (ctypes.c_void_p * 1)(buf)
         stream = torch.cuda.current_stream(cuda).cuda_stream
         for epoch in (1, 2):
-            _native.call("nnue_ft_exchange", arr, 3, fl, 1, 0, epoch, 1000, stream)
+            _native.call("nnue_ft_exchange", arr, 3, fl, 1, 0, 0, epoch, 1000, stream)
+        _native.call("nnue_ft_exchange", None, 0, fl, 1, 0, 2, 1, 1000, stream)  # channel 2: its own epochs
         torch.cuda.synchronize()
         assert _native.device_errors() == 0
         want = torch.full((37, 40), -7.0, device=cuda)
@@ -149,7 +150,9 @@ def test_exchange_copies_and_self_barrier(cuda, rows, blocks):
         assert torch.equal(got[:, :20], want.view(torch.int32)[:, :20])  # bit for bit, the NaN too
         assert torch.equal(dst[:, 20:], want[:, 20:])
         assert torch.equal(dst_i, ints)
-        assert flags[0].item() == 2 and flags[1].item() == 0  # epoch 2 seen; the block counter reset
+        # channel 0 saw epoch 2, channel 2 epoch 1; the block counters are reset
+        assert flags[0].item() == 2 and flags[15].item() == 0
+        assert flags[32].item() == 1 and flags[47].item() == 0
     finally:
         for k, v in old.items():
             _native.set_param(k, v)
@@ -170,7 +173,7 @@ def test_exchange_barrier_times_out_without_the_other_rank(cuda):
         fl = (ctypes.c_void_p * 2)(own, other)
         _native.device_errors()  # start from clear flags
         t0 = time.perf_counter()
-        _native.call("nnue_ft_exchange", None, 0, fl, 2, 0, 1, 200, torch.cuda.current_stream(cuda).cuda_stream)
+        _native.call("nnue_ft_exchange", None, 0, fl, 2, 0, 0, 1, 200, torch.cuda.current_stream(cuda).cuda_stream)
         torch.cuda.synchronize()
         assert time.perf_counter() - t0 >= 0.19
         assert _native.device_errors() == _native.DEVERR_EXCHANGE_TIMEOUT

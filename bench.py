@@ -94,6 +94,9 @@ def parse_args():
                         "buffers (the default), p2p = torch.distributed point-to-point operations")
     p.add_argument("--cols-prepare", choices=["forward", "overlap"], default="forward",
                    help="--parallel cols: where the backward's index phase runs (colsharded.ColumnShardedFT)")
+    p.add_argument("--cols-prefetch", action="store_true",
+                   help="--parallel cols: move the next step's index rows during the current step "
+                        "(ColumnShardedFT.prefetch_indices) instead of at its start")
     p.add_argument("--ddp-blocks", type=int, default=4,
                    help="N > 1: row blocks whose gradient allreduce overlaps the next block's backward "
                         "(0 = one allreduce after the whole backward)")
@@ -482,9 +485,13 @@ def run_ours(args):
         ws = plan.workspace
         dist.barrier()  # every rank arrives at its first exchange together
         plan.gather_indices(i0, i1)
-        ki0, ki1, ko0, ko1 = plan.idx[0], plan.idx[1], plan.y[0], plan.y[1]
+        # all positions' rows, a private copy for the forward-alone timing
+        kidx = plan.idx.clone()
+        if args.cols_prefetch:
+            plan.prefetch_indices(i0, i1)
+        ki0, ki1, ko0, ko1 = kidx[0], kidx[1], plan.y[0], plan.y[1]
         knnz = nnz_all
-        kcounts = torch.bincount(plan.idx[plan.idx >= 0].long(), minlength=T).cpu().numpy()
+        kcounts = torch.bincount(kidx[kidx >= 0].long(), minlength=T).cpu().numpy()
     else:
         Wk, bk, kc, kb = W, bias, C, b_rank
         ws = ops.alloc_workspace(b_rank, K, T, C, 2, dev)
@@ -499,10 +506,13 @@ def run_ours(args):
     def step_cols(e=None):
         if e:
             e[0].record()
-        plan.gather_indices(i0, i1)
+        if not args.cols_prefetch:
+            plan.gather_indices(i0, i1)
         if e:
             e[1].record()
         plan.forward_local(Wk, bk)
+        if args.cols_prefetch:
+            plan.prefetch_indices(i0, i1)  # the next step's rows (the same synthetic batch)
         if e:
             e[2].record()
         plan.exchange_outputs()
@@ -970,7 +980,8 @@ def run_ours(args):
             "data": DATA,
             "config": dict(base_config(args, world, b_rank, T, K, int(nnz_all)),
                            **({"exchange": plan.exchange, "column_slices": plan.slices,
-                               "index_phase": plan.prepare} if cols else {})),
+                               "index_phase": plan.prepare, "index_prefetch": bool(args.cols_prefetch)}
+                              if cols else {})),
             "phases_ms": phase_ms,
             "instrumented_ms_per_step": ms_instrumented,
             "roofline": roofline,

@@ -227,6 +227,8 @@ class ColumnShardedFT:
         self.workspace = self.kernels.alloc_workspace(self.B, self.K, self.T, self.width, dev)
         self._peer = None
         self._slot = 0
+        self._pending = None
+        self._pf_stream = None
         if exchange is None:
             exchange = "peer" if self._peer_capable() else "p2p"
         if exchange == "peer":
@@ -249,6 +251,11 @@ class ColumnShardedFT:
 
     # -- peer exchange setup ---------------------------------------------------
     _FLAG_BYTES = 256
+    # index-row slots: a step's rows stay in place until every rank is past
+    # that step's backward (its index phase may still read them), the next
+    # step's may be arriving (prefetch_indices), and one more is free
+    _IDX_SLOTS = 3
+    _CH_STEP, _CH_PREFETCH = 0, 1  # exchange channels
 
     def _peer_capable(self) -> bool:
         if self.device.type != "cuda" or self.world > 15 or self.C % VECTOR or self.K % VECTOR:
@@ -267,7 +274,8 @@ class ColumnShardedFT:
 
         f32 = 4
         off_idx = self._FLAG_BYTES
-        off_out = off_idx + up(2 * self.B * self.K * 4)
+        idx_slot = up(2 * self.B * self.K * 4)
+        off_out = off_idx + self._IDX_SLOTS * idx_slot
         off_d = off_out + up(2 * 2 * self.b * self.C * f32)  # two steps' outputs
         total = off_d + up(2 * self.B * max(self.widths) * f32)
         with torch.cuda.device(self.device):
@@ -287,10 +295,14 @@ class ColumnShardedFT:
                 p = ctypes.c_void_p(0)
                 _native.call("nnue_ft_exchange_open", ctypes.create_string_buffer(h, 64), ctypes.byref(p))
                 bases.append(p.value)
-        self._peer = {"base": bases, "own": base.value, "off_idx": off_idx, "off_out": off_out, "off_d": off_d,
+        self._peer = {"base": bases, "own": base.value, "off_idx": off_idx, "idx_slot": idx_slot, "off_out": off_out,
+                      "off_d": off_d,
                       "epoch": [0, 0, 0, 0], "flags": (ctypes.c_void_p * self.world)(*bases), "total": total}
         own = base.value
-        self.idx = _device_view(own + off_idx, (2, self.B, self.K), torch.int32, self.device)
+        self._idx_slots = [_device_view(own + off_idx + i * idx_slot, (2, self.B, self.K), torch.int32, self.device)
+                           for i in range(self._IDX_SLOTS)]
+        self._cur = 0
+        self.idx = self._idx_slots[0]
         self._out = [_device_view(own + off_out + i * 2 * self.b * self.C * f32, (2, self.b, self.C), torch.float32,
                                   self.device) for i in range(2)]
         self.d = _device_view(own + off_d, (2, self.B, self.width), torch.float32, self.device)
@@ -302,6 +314,8 @@ class ColumnShardedFT:
             return
         from . import _native
 
+        if self._pending is not None:  # a prefetch nobody consumed: let it land
+            self._take_prefetched()
         torch.cuda.synchronize(self.device)
         if self.world > 1:
             dist.barrier(group=self.group)  # nobody writes into a buffer after this
@@ -313,7 +327,7 @@ class ColumnShardedFT:
                 dist.barrier(group=self.group)  # every mapping of this rank's buffer is gone
             _native.call("nnue_ft_exchange_free", self._peer["own"])
         self._peer = None
-        self.idx = self.d = self._out = None
+        self.idx = self.d = self._out = self._idx_slots = None
 
     def _peer_exchange(self, copies, channel: int = 0) -> None:
         """copies: [(src_ptr, dst_ptr, rows, src_ld, dst_ld, width, scale)],
@@ -377,14 +391,13 @@ class ColumnShardedFT:
             if tuple(x.shape) != (self.b, self.K):
                 raise ValueError(f"index rows must be [{self.b}, {self.K}], got {tuple(x.shape)}")
         if self._peer is not None:
-            xs = [x.contiguous() for x in (idx0, idx1)]
-            kv = self.K // VECTOR
-            copies = []
-            for s in range(self.world):
-                for p in range(2):
-                    dst = self._peer["base"][s] + self._peer["off_idx"] + (p * self.B + self.rank * self.b) * self.K * 4
-                    copies.append((xs[p].data_ptr(), dst, self.b, kv, kv, kv, 1.0))
-            self._peer_exchange(copies)
+            if self._pending is not None:  # prefetched rows nobody used: let them land, then reuse their slot
+                torch.cuda.current_stream(self.device).wait_event(self._pending[1])
+                self._pending = None
+            slot = (self._cur + 1) % self._IDX_SLOTS
+            self._peer_exchange(self._index_copies(idx0, idx1, slot), self._CH_STEP)
+            self._cur = slot
+            self.idx = self._idx_slots[slot]
             return self.idx[0], self.idx[1]
         for p, x in enumerate((idx0, idx1)):
             if self.world == 1:
@@ -399,12 +412,58 @@ class ColumnShardedFT:
                     t.copy_(u)
         return self.idx[0], self.idx[1]
 
+    def _index_copies(self, idx0, idx1, slot):
+        xs = [x.contiguous() for x in (idx0, idx1)]
+        kv = self.K // VECTOR
+        copies = []
+        for s in range(self.world):
+            for p in range(2):
+                dst = self._peer["base"][s] + self._peer["off_idx"] + slot * self._peer["idx_slot"] + \
+                    (p * self.B + self.rank * self.b) * self.K * 4
+                copies.append((xs[p].data_ptr(), dst, self.b, kv, kv, kv, 1.0))
+        return copies
+
+    def prefetch_indices(self, idx0: torch.Tensor, idx1: torch.Tensor) -> None:
+        """Start moving the NEXT step's index rows (this rank's [b, K] per
+        perspective) to every rank, on a stream of their own beside the
+        current step's exchanges and backward; the next ``forward_local`` /
+        ``forward`` uses them (without index arguments).  Peer exchange only."""
+        if self._peer is None:
+            raise RuntimeError("prefetch_indices needs the peer exchange")
+        if self._pending is not None:
+            raise RuntimeError("index rows already prefetched")
+        for x in (idx0, idx1):
+            if tuple(x.shape) != (self.b, self.K):
+                raise ValueError(f"index rows must be [{self.b}, {self.K}], got {tuple(x.shape)}")
+        if self._pf_stream is None:
+            self._pf_stream = torch.cuda.Stream(device=self.device)
+        slot = (self._cur + 1) % self._IDX_SLOTS
+        self._pf_stream.wait_stream(torch.cuda.current_stream(self.device))  # the rows are ready
+        with torch.cuda.stream(self._pf_stream):
+            self._peer_exchange(self._index_copies(idx0, idx1, slot), self._CH_PREFETCH)
+            ev = torch.cuda.Event()
+            ev.record(self._pf_stream)
+        for x in (idx0, idx1):
+            x.record_stream(self._pf_stream)
+        self._pending = (slot, ev)
+
+    def _take_prefetched(self) -> bool:
+        if self._pending is None:
+            return False
+        slot, ev = self._pending
+        self._pending = None
+        torch.cuda.current_stream(self.device).wait_event(ev)
+        self._cur = slot
+        self.idx = self._idx_slots[slot]
+        return True
+
     # -- the step -------------------------------------------------------------
     def forward_local(self, weight_cols: torch.Tensor, bias_cols: torch.Tensor) -> None:
         """The pair forward + the backward's index phase over all positions
         (``gather_indices`` first) on this rank's columns."""
         if tuple(weight_cols.shape) != (self.T, self.width) or tuple(bias_cols.shape) != (self.width,):
             raise ValueError(f"this rank's parameters must be [{self.T}, {self.width}] and [{self.width}]")
+        self._take_prefetched()
         if self._prep_stream is None:
             self.kernels.forward_prepare(self.idx[0], self.idx[1], weight_cols, bias_cols, self.y[0], self.y[1],
                                          self.workspace)
@@ -498,12 +557,17 @@ class ColumnShardedFT:
         self.kernels.backward_apply(self.d[0], self.d[1], self.B, self.K, weight_grad_cols, bias_grad_cols,
                                     self.workspace)
 
-    def forward(self, weight_cols: torch.Tensor, bias_cols: torch.Tensor, idx0: torch.Tensor, idx1: torch.Tensor,
-                out0: Optional[torch.Tensor] = None, out1: Optional[torch.Tensor] = None):
+    def forward(self, weight_cols: torch.Tensor, bias_cols: torch.Tensor, idx0: Optional[torch.Tensor],
+                idx1: Optional[torch.Tensor], out0: Optional[torch.Tensor] = None,
+                out1: Optional[torch.Tensor] = None):
         """This rank's positions' outputs [b, C] per perspective (the
-        data-parallel forward's result) from its positions' index rows; also
-        runs the backward's index phase over the whole batch."""
-        self.gather_indices(idx0, idx1)
+        data-parallel forward's result) from its positions' index rows (None:
+        the rows ``prefetch_indices`` sent); also runs the backward's index
+        phase over the whole batch."""
+        if self._pending is None:
+            if idx0 is None or idx1 is None:
+                raise ValueError("no index rows: pass them or prefetch_indices first")
+            self.gather_indices(idx0, idx1)
         self.forward_local(weight_cols, bias_cols)
         return self.exchange_outputs(out0, out1)
 
@@ -527,6 +591,7 @@ class SparseLinearPairColumnSharded(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, feature_indices_0, feature_indices_1, weight_cols, bias_cols, sharded: ColumnShardedFT):
+        # None index rows: the rows sharded.prefetch_indices already sent
         out0, out1 = sharded.forward(weight_cols, bias_cols, feature_indices_0, feature_indices_1)
         ctx.sharded = sharded
         ctx.shapes = (tuple(weight_cols.shape), weight_cols.device)

@@ -100,6 +100,37 @@ def test_single_process_equals_pair_function(cuda, exchange, prepare):
     sh.close()
 
 
+def test_single_process_prefetched_indices(cuda):
+    """Index rows sent ahead with prefetch_indices (three steps, the slots
+    rotating): the same outputs and gradients as passing them each step."""
+    from stockfish_trainer_b200 import colsharded
+
+    B, C = 2048, 264
+    white, black, W, bias, g, T, K = _inputs(B, C, seed=13)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    i0, i1 = t(white), t(black)
+    res = []
+    for prefetch in (False, True):
+        sh = colsharded.ColumnShardedFT(T, C, B, K, device=cuda, prepare="overlap")
+        Wp, bp = t(W).requires_grad_(), t(bias).requires_grad_()
+        if prefetch:
+            sh.prefetch_indices(i0, i1)
+        steps = []
+        for _ in range(3):
+            Wp.grad = bp.grad = None
+            o0, o1 = colsharded.SparseLinearPairColumnSharded.apply(None if prefetch else i0, None if prefetch else i1,
+                                                                    Wp, bp, sh)
+            if prefetch:
+                sh.prefetch_indices(i0, i1)
+            torch.autograd.backward([o0, o1], [t(g[0]), t(g[1])])
+            steps.append((o0.detach().clone(), o1.detach().clone(), Wp.grad.clone(), bp.grad.clone()))
+        res.append(steps)
+        sh.close()
+    for a, b in zip(res[0], res[1]):
+        for x, y in zip(a, b):
+            assert torch.equal(x, y)
+
+
 def _exchange_buffer(nbytes):
     import ctypes
 

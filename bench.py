@@ -92,11 +92,11 @@ def parse_args():
     p.add_argument("--exchange", choices=["peer", "p2p"], default=None,
                    help="--parallel cols: peer = this library's exchange kernel storing into the other GPUs' "
                         "buffers (the default), p2p = torch.distributed point-to-point operations")
-    p.add_argument("--cols-prepare", choices=["forward", "overlap"], default="forward",
+    p.add_argument("--cols-prepare", choices=["forward", "overlap"], default="overlap",
                    help="--parallel cols: where the backward's index phase runs (colsharded.ColumnShardedFT)")
-    p.add_argument("--cols-prefetch", action="store_true",
-                   help="--parallel cols: move the next step's index rows during the current step "
-                        "(ColumnShardedFT.prefetch_indices) instead of at its start")
+    p.add_argument("--cols-prefetch", type=int, choices=[0, 1], default=1,
+                   help="--parallel cols: 1 = move the next step's index rows during the current step "
+                        "(ColumnShardedFT.prefetch_indices), 0 = at its start")
     p.add_argument("--ddp-blocks", type=int, default=4,
                    help="N > 1: row blocks whose gradient allreduce overlaps the next block's backward "
                         "(0 = one allreduce after the whole backward)")
@@ -477,6 +477,11 @@ def run_ours(args):
         # this rank's kernels read its column slice of the table and run over
         # every position of the global batch
         from stockfish_trainer_b200 import colsharded
+
+        if not any(kv.startswith("bwd_heavy_first=") for kv in args.param):
+            # light rows on a narrow slice are short: start the heavy rows' long
+            # walks first on the side stream (4 x B200 slice: 0.52 ms against 0.55)
+            _native.set_param("bwd_heavy_first", 1)
 
         plan = colsharded.ColumnShardedFT(T, C, args.batch, K, device=dev, exchange=args.exchange,
                                           prepare=args.cols_prepare)
@@ -980,7 +985,8 @@ def run_ours(args):
             "data": DATA,
             "config": dict(base_config(args, world, b_rank, T, K, int(nnz_all)),
                            **({"exchange": plan.exchange, "column_slices": plan.slices,
-                               "index_phase": plan.prepare, "index_prefetch": bool(args.cols_prefetch)}
+                               "index_phase": plan.prepare, "index_prefetch": bool(args.cols_prefetch),
+                               "bwd_heavy_first": _native.get_param("bwd_heavy_first")}
                               if cols else {})),
             "phases_ms": phase_ms,
             "instrumented_ms_per_step": ms_instrumented,

@@ -868,6 +868,8 @@ __global__ void __launch_bounds__(128, 8) ft_segsum_tail_kernel(const SegParams 
 // zeroed before the launch; nobody waits) writes dW = acc_white + acc_black.
 constexpr int kHeavyWarps = 2;
 constexpr int kHeavyStages = 48;
+constexpr int kHeavyBatch = 8;
+static_assert(kHeavyStages % kHeavyBatch == 0, "a batch never wraps the ring");
 
 template <typename VT>
 __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const SegParams p) {
@@ -912,7 +914,23 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
     ++t;
   };
   for (int i = 0; i < kHeavyStages; ++i) issue(i);
-  for (int j = s, stage = 0; j < e; ++j) {
+  int j = s, stage = 0;
+  // kHeavyBatch entries at a time: their ring slots read together, then added
+  // in order, then re-issued -- one shared-memory round trip per batch
+  // instead of one per entry (the walk is a chain of dependent steps)
+  for (; j + kHeavyBatch <= e; j += kHeavyBatch) {
+    cp_async_wait<kHeavyStages - kHeavyBatch>();  // the batch's groups (the oldest) have landed
+    VT v[kHeavyBatch];
+#pragma unroll
+    for (int b = 0; b < kHeavyBatch; ++b) v[b] = ring[(stage + b) * 32];
+#pragma unroll
+    for (int b = 0; b < kHeavyBatch; ++b) Ops::add(acc, v[b]);
+    __syncwarp();
+#pragma unroll
+    for (int b = 0; b < kHeavyBatch; ++b) issue(stage + b);
+    stage = stage + kHeavyBatch == kHeavyStages ? 0 : stage + kHeavyBatch;
+  }
+  for (; j < e; ++j) {
     cp_async_wait<kHeavyStages - 1>();
     Ops::add(acc, ring[stage * 32]);
     __syncwarp();

@@ -898,46 +898,49 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) ft_segsum_heavy_kernel(const
     return base + lane < e ? decode_position(__ldg(p.sorted_b + base + lane), q, p.B) : -1;
   };
   VT acc = Ops::zero();
+  // Entries move in batches of kHeavyBatch, one cp.async group each: the
+  // batch's positions come from one group of 32 decoded positions (a batch
+  // never straddles two: 32 is a multiple of the batch), its shuffles and
+  // copies are issued back to back, and the consume side reads the batch's
+  // ring slots together and adds them in order -- the walk costs one chain
+  // of dependent steps per batch instead of per entry.
   int t = s;  // issue pointer, kHeavyStages entries ahead of the consume pointer
   int g_base = s, g_cur = group(s), g_next = group(s + 32);
-  auto issue = [&](int slot_i) {
-    if (t < e) {
-      if (t - g_base == 32) {  // next group of positions: already loaded; load the one after
-        g_base += 32;
-        g_cur = g_next;
-        g_next = group(g_base + 32);
-      }
-      const int b = __shfl_sync(kFull, g_cur, t - g_base);
-      cp_async_vec<VT>(ring + slot_i * 32, src + (b >= 0 ? (int64_t)b * row_vec : 0), ok1 && b >= 0);
+  auto issue_batch = [&](int slot0) {
+    if (t - g_base == 32) {  // next group of positions: already loaded; load the one after
+      g_base += 32;
+      g_cur = g_next;
+      g_next = group(g_base + 32);
     }
-    cp_async_commit();  // empty groups keep the pending count constant
-    ++t;
+    const int o = t - g_base;  // 0, 8, 16 or 24
+    int b[kHeavyBatch];
+#pragma unroll
+    for (int k = 0; k < kHeavyBatch; ++k) b[k] = __shfl_sync(kFull, g_cur, o + k);
+#pragma unroll
+    for (int k = 0; k < kHeavyBatch; ++k)
+      if (t + k < e)  // past the segment: the slot is never read
+        cp_async_vec<VT>(ring + (slot0 + k) * 32, src + (b[k] >= 0 ? (int64_t)b[k] * row_vec : 0), ok1 && b[k] >= 0);
+    cp_async_commit();
+    t += kHeavyBatch;
   };
-  for (int i = 0; i < kHeavyStages; ++i) issue(i);
+  for (int i = 0; i < kHeavyStages / kHeavyBatch; ++i) issue_batch(i * kHeavyBatch);
   int j = s, stage = 0;
-  // kHeavyBatch entries at a time: their ring slots read together, then added
-  // in order, then re-issued -- one shared-memory round trip per batch
-  // instead of one per entry (the walk is a chain of dependent steps)
   for (; j + kHeavyBatch <= e; j += kHeavyBatch) {
-    cp_async_wait<kHeavyStages - kHeavyBatch>();  // the batch's groups (the oldest) have landed
+    cp_async_wait<kHeavyStages / kHeavyBatch - 1>();  // the oldest batch has landed
     VT v[kHeavyBatch];
 #pragma unroll
-    for (int b = 0; b < kHeavyBatch; ++b) v[b] = ring[(stage + b) * 32];
+    for (int k = 0; k < kHeavyBatch; ++k) v[k] = ring[(stage + k) * 32];
 #pragma unroll
-    for (int b = 0; b < kHeavyBatch; ++b) Ops::add(acc, v[b]);
+    for (int k = 0; k < kHeavyBatch; ++k) Ops::add(acc, v[k]);
     __syncwarp();
-#pragma unroll
-    for (int b = 0; b < kHeavyBatch; ++b) issue(stage + b);
+    issue_batch(stage);
     stage = stage + kHeavyBatch == kHeavyStages ? 0 : stage + kHeavyBatch;
   }
+  cp_async_wait<0>();  // the last, partial batch (already issued)
   for (; j < e; ++j) {
-    cp_async_wait<kHeavyStages - 1>();
     Ops::add(acc, ring[stage * 32]);
-    __syncwarp();
-    issue(stage);
-    stage = stage + 1 == kHeavyStages ? 0 : stage + 1;
+    ++stage;  // < kHeavyBatch entries from a batch-aligned slot: no wrap
   }
-  cp_async_wait<0>();
   const bool ok[1] = {ok1};
   if (P == 1) {
     const VT t1[1] = {acc};

@@ -479,9 +479,11 @@ def run_ours(args):
         # every position of the global batch
         from stockfish_trainer_b200 import colsharded
 
-        if not any(kv.startswith("bwd_heavy_first=") for kv in args.param):
-            # light rows on a narrow slice are short: start the heavy rows' long
-            # walks first on the side stream (4 x B200 slice: 0.52 ms against 0.55)
+        if world >= 8 and not any(kv.startswith("bwd_heavy_first=") for kv in args.param):
+            # light rows on an 8-way slice are short: start the heavy rows'
+            # walks first on the side stream (one B200, the 136-column slice over
+            # 65536 positions: backward 0.336 ms against 0.356; the 264-column
+            # slice of 4 GPUs: 0.432 against 0.424, so only from 8)
             _native.set_param("bwd_heavy_first", 1)
 
         plan = colsharded.ColumnShardedFT(T, C, args.batch, K, device=dev, exchange=args.exchange,

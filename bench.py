@@ -95,9 +95,10 @@ def parse_args():
                         "buffers (the default), p2p = torch.distributed point-to-point operations")
     p.add_argument("--cols-prepare", choices=["forward", "overlap"], default="overlap",
                    help="--parallel cols: where the backward's index phase runs (colsharded.ColumnShardedFT)")
-    p.add_argument("--cols-prefetch", type=int, choices=[0, 1], default=1,
-                   help="--parallel cols: 1 = move the next step's index rows during the current step "
-                        "(ColumnShardedFT.prefetch_indices), 0 = at its start")
+    p.add_argument("--cols-prefetch", type=int, choices=[0, 1, 2], default=1,
+                   help="--parallel cols: move the next step's index rows during the current step "
+                        "(ColumnShardedFT.prefetch_indices) -- 1: issued after the forward, 2: after the "
+                        "gradient exchange (beside the backward) -- or 0: at the step's start")
     p.add_argument("--ddp-blocks", type=int, default=4,
                    help="N > 1: row blocks whose gradient allreduce overlaps the next block's backward "
                         "(0 = one allreduce after the whole backward)")
@@ -519,7 +520,7 @@ def run_ours(args):
         if e:
             e[1].record()
         plan.forward_local(Wk, bk)
-        if args.cols_prefetch:
+        if args.cols_prefetch == 1:
             plan.prefetch_indices(i0, i1)  # the next step's rows (the same synthetic batch)
         if e:
             e[2].record()
@@ -527,6 +528,8 @@ def run_ours(args):
         if e:
             e[3].record()
         plan.exchange_grads(g0, g1)
+        if args.cols_prefetch == 2:
+            plan.prefetch_indices(i0, i1)
         if e:
             e[4].record()
         plan.backward_local(grads.weight, grads.bias)

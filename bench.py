@@ -89,13 +89,14 @@ def parse_args():
                         "outputs and output gradients (stockfish_trainer_b200.colsharded); dp = every rank "
                         "holds the whole table and the weight gradient is allreduce-averaged (the reference's "
                         "DDP scheme); auto = dp below 4 GPUs, cols from 4 (on B200s: 2 GPUs dp 30.6 against "
-                        "cols 25.0 M positions/s, 4 GPUs dp 37.5 against cols 39.3)")
+                        "cols 25.0 M positions/s, 4 GPUs dp 37.5 against cols 42.8, 8 GPUs dp 39.1 against "
+                        "cols 58.8)")
     p.add_argument("--exchange", choices=["peer", "p2p"], default=None,
                    help="--parallel cols: peer = this library's exchange kernel storing into the other GPUs' "
                         "buffers (the default), p2p = torch.distributed point-to-point operations")
     p.add_argument("--cols-prepare", choices=["forward", "overlap"], default="overlap",
                    help="--parallel cols: where the backward's index phase runs (colsharded.ColumnShardedFT)")
-    p.add_argument("--cols-prefetch", type=int, choices=[0, 1, 2], default=1,
+    p.add_argument("--cols-prefetch", type=int, choices=[0, 1, 2], default=2,
                    help="--parallel cols: move the next step's index rows during the current step "
                         "(ColumnShardedFT.prefetch_indices) -- 1: issued after the forward, 2: after the "
                         "gradient exchange (beside the backward) -- or 0: at the step's start")

@@ -232,12 +232,17 @@ class ColumnShardedFT:
         self._slot = 0
         self._pending = None
         self._pf_stream = None
-        if exchange is None:
-            exchange = "peer" if self._peer_capable() else "p2p"
-        if exchange == "peer":
-            self._setup_peer_exchange()
-        elif exchange != "p2p":
+        if exchange not in (None, "peer", "p2p"):
             raise ValueError(f"exchange must be 'peer' or 'p2p', got {exchange!r}")
+        if exchange == "peer" or (exchange is None and self._peer_capable()):
+            err = self._setup_peer_exchange()
+            if err is not None:  # every rank saw the same failure (a collective): all fall back or all raise
+                if exchange == "peer":
+                    raise RuntimeError(f"peer exchange unavailable: {err}")
+                exchange = "p2p"
+            else:
+                exchange = "peer"
+        exchange = exchange or "p2p"
         self.exchange = exchange
         if exchange == "p2p":
             # all positions' index rows, per perspective [B, K]
@@ -267,7 +272,10 @@ class ColumnShardedFT:
             return True
         return dist.get_backend(self.group) == "nccl"
 
-    def _setup_peer_exchange(self) -> None:
+    def _setup_peer_exchange(self) -> Optional[str]:
+        """Allocate, share and map the exchange buffers; None on success, else
+        the first rank's error (every rank returns the same, having undone
+        its own allocations and mappings)."""
         import ctypes
 
         from . import _native
@@ -290,14 +298,30 @@ class ColumnShardedFT:
                 dist.all_gather_object(handles, handle.raw, group=self.group)
             else:
                 handles[0] = handle.raw
-            bases = []
+            bases, err = [], None
             for s, h in enumerate(handles):
                 if s == self.rank:
                     bases.append(base.value)
                     continue
                 p = ctypes.c_void_p(0)
-                _native.call("nnue_ft_exchange_open", ctypes.create_string_buffer(h, 64), ctypes.byref(p))
+                try:
+                    _native.call("nnue_ft_exchange_open", ctypes.create_string_buffer(h, 64), ctypes.byref(p))
+                except _native.NativeError as e:
+                    err = f"rank {self.rank} mapping rank {s}'s buffer: {e}"
+                    break
                 bases.append(p.value)
+            errs = [err] * self.world
+            if self.world > 1:
+                dist.all_gather_object(errs, err, group=self.group)
+            first = next((e for e in errs if e), None)
+            if first is not None:
+                for s, b in enumerate(bases):
+                    if s != self.rank:
+                        _native.call("nnue_ft_exchange_close", b)
+                if self.world > 1:
+                    dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+                _native.call("nnue_ft_exchange_free", base.value)
+                return first
         self._peer = {"base": bases, "own": base.value, "off_idx": off_idx, "idx_slot": idx_slot, "off_out": off_out,
                       "off_d": off_d,
                       "epoch": [0, 0, 0, 0], "flags": (ctypes.c_void_p * self.world)(*bases), "total": total}
@@ -309,6 +333,7 @@ class ColumnShardedFT:
         self._out = [_device_view(own + off_out + i * 2 * self.b * self.C * f32, (2, self.b, self.C), torch.float32,
                                   self.device) for i in range(2)]
         self.d = _device_view(own + off_d, (2, self.B, self.width), torch.float32, self.device)
+        return None
 
     def close(self) -> None:
         """Unmap the other ranks' exchange buffers and free this rank's (a

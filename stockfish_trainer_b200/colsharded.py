@@ -234,6 +234,9 @@ class ColumnShardedFT:
         self._pf_stream = None
         if exchange not in (None, "peer", "p2p"):
             raise ValueError(f"exchange must be 'peer' or 'p2p', got {exchange!r}")
+        if exchange == "peer" and not self._peer_capable():
+            raise ValueError("the peer exchange needs CUDA tensors in an NCCL group of at most 15 ranks with "
+                             "output_size and max_active multiples of 4; use exchange='p2p'")
         if exchange == "peer" or (exchange is None and self._peer_capable()):
             err = self._setup_peer_exchange()
             if err is not None:  # every rank saw the same failure (a collective): all fall back or all raise

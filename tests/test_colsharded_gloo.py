@@ -147,3 +147,17 @@ def test_column_slices():
             assert max(widths) - min(widths) <= 2 * colsharded.CHUNK
     # columns not a multiple of 4: an even split
     assert colsharded.column_slices(10, 3) == [(0, 3), (3, 6), (6, 10)]
+
+
+def test_exchange_choice_on_cpu():
+    """Without CUDA the point-to-point exchange is chosen; asking for the peer
+    exchange is refused with a clear error instead of reaching CUDA."""
+    sys.path.insert(0, ROOT)
+    from stockfish_trainer_b200 import colsharded
+
+    sh = colsharded.ColumnShardedFT(T, C, B, K, device="cpu", kernels=_OracleKernels())
+    assert (sh.exchange, sh.prepare, sh.world) == ("p2p", "forward", 1)
+    with pytest.raises(ValueError, match="peer exchange"):
+        colsharded.ColumnShardedFT(T, C, B, K, device="cpu", kernels=_OracleKernels(), exchange="peer")
+    with pytest.raises(ValueError):
+        colsharded.ColumnShardedFT(T, C, B, K, device="cpu", kernels=_OracleKernels(), exchange="nvls")

@@ -161,3 +161,43 @@ def test_exchange_choice_on_cpu():
         colsharded.ColumnShardedFT(T, C, B, K, device="cpu", kernels=_OracleKernels(), exchange="peer")
     with pytest.raises(ValueError):
         colsharded.ColumnShardedFT(T, C, B, K, device="cpu", kernels=_OracleKernels(), exchange="nvls")
+
+
+def _worker_dead_rank(rank, world, port, out_dir):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from stockfish_trainer_b200 import colsharded, ddp
+
+    ddp.init_from_env("gloo", timeout_s=5)
+    W, bias, idx, g = _inputs()
+    sh = colsharded.ColumnShardedFT(T, C, B, K, device="cpu", kernels=_OracleKernels())
+    b = B // world
+    lo = rank * b
+    sh.forward(sh.shard_columns(torch.from_numpy(W)), sh.shard_columns(torch.from_numpy(bias)),
+               torch.from_numpy(idx[0, lo:lo + b].copy()), torch.from_numpy(idx[1, lo:lo + b].copy()))
+    if rank == 1:
+        os._exit(0)  # leaves between the forward and the backward, before its exchange
+    try:
+        dW, dB = torch.empty(T, sh.width), torch.empty(sh.width)
+        sh.backward(torch.from_numpy(g[0, lo:lo + b].copy()), torch.from_numpy(g[1, lo:lo + b].copy()), dW, dB)
+        result = "completed"
+    except Exception as e:  # gloo reports the missing peer
+        result = "error: " + type(e).__name__
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(result)
+    os._exit(0)
+
+
+def test_dead_rank_is_detected_not_hung(tmp_path):
+    """A rank that leaves between steps: the other's next exchange ends with
+    an error within the process group's timeout instead of waiting forever."""
+    ctx = mp.start_processes(_worker_dead_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(timeout=120)
+    alive = [p for p in ctx.processes if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung waiting for a dead peer"
+    assert (tmp_path / "r0.txt").read_text().startswith("error")

@@ -469,12 +469,15 @@ class ColumnShardedFT:
         if self._pf_stream is None:
             self._pf_stream = torch.cuda.Stream(device=self.device)
         slot = (self._cur + 1) % self._IDX_SLOTS
+        # contiguous rows made on the current stream; the prefetch stream reads
+        # them, so the caching allocator must not reuse them before it has
+        xs = [x.contiguous() for x in (idx0, idx1)]
         self._pf_stream.wait_stream(torch.cuda.current_stream(self.device))  # the rows are ready
         with torch.cuda.stream(self._pf_stream):
-            self._peer_exchange(self._index_copies(idx0, idx1, slot), self._CH_PREFETCH)
+            self._peer_exchange(self._index_copies(xs[0], xs[1], slot), self._CH_PREFETCH)
             ev = torch.cuda.Event()
             ev.record(self._pf_stream)
-        for x in (idx0, idx1):
+        for x in xs:
             x.record_stream(self._pf_stream)
         self._pending = (slot, ev)
 
@@ -593,12 +596,15 @@ class ColumnShardedFT:
                 out1: Optional[torch.Tensor] = None):
         """This rank's positions' outputs [b, C] per perspective (the
         data-parallel forward's result) from its positions' index rows (None:
-        the rows ``prefetch_indices`` sent); also runs the backward's index
-        phase over the whole batch."""
-        if self._pending is None:
-            if idx0 is None or idx1 is None:
-                raise ValueError("no index rows: pass them or prefetch_indices first")
-            self.gather_indices(idx0, idx1)
+        the rows ``prefetch_indices`` sent; rows passed here take precedence
+        over a pending prefetch); also runs the backward's index phase over
+        the whole batch."""
+        if (idx0 is None) != (idx1 is None):
+            raise ValueError("pass both perspectives' index rows or neither")
+        if idx0 is not None:
+            self.gather_indices(idx0, idx1)  # lets a pending prefetch land first, then replaces it
+        elif self._pending is None:
+            raise ValueError("no index rows: pass them or prefetch_indices first")
         self.forward_local(weight_cols, bias_cols)
         return self.exchange_outputs(out0, out1)
 

@@ -131,6 +131,29 @@ def test_single_process_prefetched_indices(cuda):
             assert torch.equal(x, y)
 
 
+def test_explicit_rows_take_precedence_over_a_prefetch(cuda):
+    """Rows passed to the step win over different rows sent ahead with
+    prefetch_indices (which still land first); with None the prefetched rows
+    are used."""
+    from stockfish_trainer_b200 import colsharded, positions
+
+    B, C = 1024, 264
+    white, black, W, bias, g, T, K = _inputs(B, C, seed=17)
+    w2, b2, _ = positions.synthetic_batch(B, FS, seed=18)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    Wd, bd = t(W), t(bias)
+    sh = colsharded.ColumnShardedFT(T, C, B, K, device=cuda)
+    want_a = [x.clone() for x in sh.forward(Wd, bd, t(white), t(black))]
+    want_b = [x.clone() for x in sh.forward(Wd, bd, t(w2), t(b2))]
+    sh.prefetch_indices(t(w2), t(b2))
+    got = [x.clone() for x in sh.forward(Wd, bd, t(white), t(black))]  # explicit rows win
+    assert all(torch.equal(a, b) for a, b in zip(got, want_a))
+    sh.prefetch_indices(t(w2), t(b2))
+    got = [x.clone() for x in sh.forward(Wd, bd, None, None)]  # the prefetched rows
+    assert all(torch.equal(a, b) for a, b in zip(got, want_b))
+    sh.close()
+
+
 def _exchange_buffer(nbytes):
     import ctypes
 
